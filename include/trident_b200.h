@@ -1,0 +1,168 @@
+/*
+ * trident_b200 — C ABI of the B200 (sm_100a) TRIDENT lossless IVF query path.
+ *
+ * The reference exposes this path as one pybind11 call,
+ *   launch_trident_v4_search(mode, tile_size, use_l1, per_cluster_sq8, rerank_m, nprobe, xq_orig,
+ *                            W_combined, ..., topk_d, topk_i, ..., record_events, warp_refine,
+ *                            stats_buf, r_vec_sorted) -> float ms
+ * (src/trident_v4_kernels.cu:1172-1217, bound at :1606-1627), called by TridentV4Index.search
+ * (benchmarks/phase4a_suite.py:280-342). The entry points below replace that call and its pieces.
+ * They take plain pointers and sizes only; the caller owns every buffer (index arrays, workspace,
+ * outputs), as in the reference, and no entry point allocates device memory.
+ *
+ * Conventions shared by every entry point:
+ *  - return TRIDENT_OK (0) or a TRIDENT_ERR_* code; trident_last_error() gives the message of the
+ *    calling thread's last failure (the reference surfaced no errors at all);
+ *  - all work is queued on `stream` (a cudaStream_t; NULL = the legacy default stream) and is
+ *    asynchronous, like the reference, which ran on torch's current stream (:1231);
+ *  - one workspace must not be used by two searches that overlap in time (the reference's scratch
+ *    buffers had the same restriction).
+ */
+#ifndef TRIDENT_B200_H
+#define TRIDENT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TRIDENT_ABI_VERSION 1
+
+enum trident_status {
+    TRIDENT_OK = 0,
+    TRIDENT_ERR_INVALID = 1,     /* bad argument, shape or pointer                      */
+    TRIDENT_ERR_WORKSPACE = 2,   /* workspace smaller than trident_workspace_size()     */
+    TRIDENT_ERR_CUDA = 3,        /* a CUDA runtime call or kernel launch failed         */
+    TRIDENT_ERR_UNSUPPORTED = 4  /* a mode or shape this build does not implement       */
+};
+
+/* Search modes; the values are the reference's `mode` argument (:1173). */
+enum trident_mode {
+    TRIDENT_MODE_AUTO = -1,      /* cost router: CM-FP32 if W < w0 else cascade (phase4a_suite.py:1079) */
+    TRIDENT_MODE_CASCADE = 2,    /* K2: Stage X warm-up, Stage Y SQ8 lower bound, Stage Z FP32 refine   */
+    TRIDENT_MODE_CM_FP32 = 10    /* exact cluster-major FP32 scan of every probed row                   */
+};
+
+/* Index arrays on the device (xb_sorted may instead be mapped pinned host memory: the zero-copy
+ * out-of-core mode). They carry the semantics of the reference's SharedClusterStorage and
+ * TridentV4Index arrays (phase4a_suite.py:75-255) in a B200 layout:
+ *   codes    [total_tiles][num_blocks][tile_size][32] u8: tile t of list c holds rows
+ *            list_row_off[c] + (t - list_tile_off[c]) * tile_size + v, 32 dims per block; one
+ *            32-dim block of one row is one 32-byte DRAM sector (reference layout:
+ *            sq8_packed [tiles][D4][W][32] u32, :189-230);
+ *   vmin/delta [nlist][D_pad]: per-list SQ8 interval, codes = clip(round((x~ - vmin)/delta),0,255)
+ *            of the float32 PCA-rotated row x~ (phase4a_suite.py:157-179);
+ *   eps      [nlist][D_pad]: rigorous per-dim bound on |x~ - (vmin + code*delta)| plus the float32
+ *            rounding of the bound's arithmetic (the reference used 0.5001*delta, :179). */
+typedef struct trident_index {
+    int64_t N;                       /* rows                                             */
+    int32_t D;                       /* dimension                                        */
+    int32_t D_pad;                   /* ceil(D/32)*32                                    */
+    int32_t nlist;                   /* IVF lists                                        */
+    int32_t tile_size;               /* rows per tile: 128 or 256                        */
+    int32_t num_blocks;              /* D_pad / 32                                       */
+    int32_t reserved0;
+    const float*   xb_sorted;        /* [N, D] rows in list order                        */
+    const int32_t* orig_ids_sorted;  /* [N] original id of each sorted row               */
+    const int64_t* list_row_off;     /* [nlist+1] (reference: cluster_vec_off, int32)    */
+    const int64_t* list_tile_off;    /* [nlist+1] (reference: cluster_tile_off)          */
+    const uint8_t* codes;            /* blocked SQ8 codes, see above                     */
+    const float*   vmin;             /* [nlist, D_pad]                                   */
+    const float*   delta;            /* [nlist, D_pad]                                   */
+    const float*   eps;              /* [nlist, D_pad]                                   */
+    const float*   centroids;        /* [nlist, D]                                       */
+    const float*   centroid_norm_sq; /* [nlist] ||c||^2 rounded from float64             */
+    const double*  pca_mean;         /* [D]                                              */
+    const double*  pca_rot;          /* [D, D] row-major; column d is component d        */
+    float centroid_norm_max;         /* max_c ||c||, for the coarse GEMM error bound     */
+    float lb_rel_slack;              /* relative slack rho of the Stage-Y prune test     */
+} trident_index;
+
+/* Statistics slots of the optional int64 `stats` array (at least TRIDENT_STATS_LEN entries, zeroed
+ * by the caller). Slots 0-3 are the reference's stats_buf counters (:700-704, :774-795, :921-923). */
+enum trident_stat_slot {
+    TRIDENT_STAT_CANDIDATES = 0,     /* (query, row) pairs entering Stage Y                     */
+    TRIDENT_STAT_SCANNED_DIMS = 1,   /* dimensions scanned by Stage Y                           */
+    TRIDENT_STAT_SURVIVORS = 2,      /* pairs reaching Stage Z (exact FP32)                     */
+    TRIDENT_STAT_INSERTED = 3,       /* refined rows inserted into a per-query top-K            */
+    TRIDENT_STAT_COARSE_RECHECK = 4, /* lists re-checked in float64 at the nprobe boundary      */
+    TRIDENT_STAT_ITEMS = 5,          /* (list, query-group) work items processed                */
+    TRIDENT_STATS_LEN = 8
+};
+
+/* Version of this ABI (TRIDENT_ABI_VERSION). */
+int trident_version(void);
+
+/* Message of the calling thread's last failed call ("" if none). */
+const char* trident_last_error(void);
+
+/* Checks the index descriptor (shapes, tile size, alignment of the row array). */
+int trident_index_check(const trident_index* idx);
+
+/* Workspace bytes a search of (B, K, nprobe) needs. Replaces the reference's preallocated
+ * scratch tensors (proj_buf ... cand_cnt, phase4a_suite.py:257-278). */
+int trident_workspace_size(const trident_index* idx, int32_t B, int32_t K, int32_t nprobe,
+                           size_t* bytes);
+
+/* The warm-up split m_warm (p_init) the reference uses for mode 2 (:1264-1276). */
+int32_t trident_p_init(int32_t mode, int32_t B, int32_t K, int32_t nprobe);
+
+/* The cost router (phase4a_suite.py:1013-1035, 1079): returns TRIDENT_MODE_CM_FP32 when
+ * W = B * nprobe * (N / nlist) * D < w0, else TRIDENT_MODE_CASCADE. w0 <= 0 selects 9.0e8. */
+int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, double w0);
+
+/* The whole query path, replacing launch_trident_v4_search (:1172-1604):
+ *   xq       [B, D] float32 queries on the device;
+ *   K        1..100 (the reference supported K = 10 only, :575, :984);
+ *   mode     TRIDENT_MODE_{AUTO, CASCADE, CM_FP32};
+ *   ub_seed  0: warm-up lists only; 1: also seed the warm-up lists' threshold from SQ8 upper
+ *            bounds; 2: seed every pass (the reference's TRIDENT_UB_SEED, :1262, now an argument);
+ *   out_d    [B, K] float32 squared distances ascending; out_i [B, K] int64 original ids;
+ *            ties are broken by the smaller id; missing results are (+inf, -1);
+ *   stats    optional int64[TRIDENT_STATS_LEN] accumulated counters (NULL to skip). */
+int trident_search(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
+                   int32_t mode, int32_t ub_seed, void* workspace, size_t workspace_bytes,
+                   float* out_d, int64_t* out_i, int64_t* stats, void* stream);
+
+/* Phases timed by trident_search_profiled. */
+enum trident_phase {
+    TRIDENT_PHASE_COARSE = 0,   /* rotation + coarse GEMM + exact probe selection   */
+    TRIDENT_PHASE_PAIRS = 1,    /* cluster-major pair lists and work items          */
+    TRIDENT_PHASE_SCAN0 = 2,    /* warm-up scan over the p_init nearest lists        */
+    TRIDENT_PHASE_MERGE0 = 3,   /* warm-up merge -> per-query threshold              */
+    TRIDENT_PHASE_SCAN1 = 4,    /* main scan over the remaining lists                */
+    TRIDENT_PHASE_MERGE1 = 5,   /* final top-K merge                                 */
+    TRIDENT_PHASES = 6
+};
+
+/* trident_search plus CUDA-event timing of each phase (milliseconds, 0 for a phase that did not
+ * run), like the reference's record_events (:1291-1296, :1595-1603). It synchronises `stream`
+ * before returning. */
+int trident_search_profiled(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
+                            int32_t mode, int32_t ub_seed, void* workspace, size_t workspace_bytes,
+                            float* out_d, int64_t* out_i, int64_t* stats, void* stream,
+                            float* phase_ms);
+
+/* Number of kernels the library has launched from the calling thread so far. */
+int64_t trident_launch_count(void);
+
+/* The coarse stage alone (query PCA rotation + exact top-nprobe list selection), replacing the
+ * addmm_out + trident_topk_centroids_kernel pair (:1233-1259). probe_cids [B, nprobe] int32 comes
+ * out ascending by (float64 ||q - c||^2, list id); probe_d64 [B, nprobe] (optional) holds those
+ * float64 distances; qrot [B, D_pad] (optional) the float32-rounded rotated queries. */
+int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t nprobe,
+                   void* workspace, size_t workspace_bytes, int32_t* probe_cids, double* probe_d64,
+                   float* qrot, int64_t* stats, void* stream);
+
+/* Multi-GPU merge: R per-shard result lists d_in/i_in [R, B, K] (as gathered by an NCCL
+ * all-gather) -> the global top-K per query under the (distance, id) order. */
+int trident_merge_shards(const float* d_in, const int64_t* i_in, int32_t R, int32_t B, int32_t K,
+                         float* out_d, int64_t* out_i, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TRIDENT_B200_H */

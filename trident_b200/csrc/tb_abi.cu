@@ -1,0 +1,317 @@
+// C ABI of trident_b200: argument checks, workspace carve-up and the launch sequence of one search.
+//
+// Launch sequence of trident_search (all on the caller's stream, asynchronous), replacing
+// launch_trident_v4_search (src/trident_v4_kernels.cu:1172-1604):
+//   rotate_f64 -> coarse_gemm -> probe_select                   (coarse stage, exact probe set)
+//   pair_hist -> pair_scan -> pair_scatter -> item_emit          (cluster-major work items)
+//   [pass 0: scan over the p_init nearest lists -> merge -> tau]  (Stage X warm-up)
+//   pass 1: scan over the remaining lists -> merge -> out        (Stage Y/Z or CM-FP32)
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "tb_internal.h"
+#include "trident_b200.h"
+
+namespace {
+
+thread_local std::string g_err;
+thread_local int64_t g_launches = 0;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+    return fail(TRIDENT_ERR_CUDA, "%s: %s (%s)", where, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+constexpr int kMaxD = 4096;
+constexpr int kMaxK = 100;
+constexpr int kMaxNprobe = 1024;
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+namespace tb {
+
+int num_sms() {
+    static int cached[64] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    if (cached[dev] == 0) {
+        int n = 0;
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        cached[dev] = n > 0 ? n : 1;
+    }
+    return cached[dev];
+}
+
+size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void* base, Workspace* ws) {
+    size_t off = 0;
+    char* p = static_cast<char*>(base);
+    auto take = [&](size_t bytes) -> void* {
+        void* r = p ? (void*)(p + off) : nullptr;
+        off += align256(bytes);
+        return r;
+    };
+    const size_t Bs = (size_t)(B > 0 ? B : 1);
+    const size_t pairs = Bs * (size_t)nprobe;
+    Workspace w;
+    w.qrot = (float*)take(Bs * idx.D_pad * sizeof(float));
+    w.qinfo = (float*)take(Bs * QI_LEN * sizeof(float));
+    w.coarse = (float*)take(Bs * (size_t)idx.nlist * sizeof(float));
+    w.probe = (int32_t*)take(pairs * sizeof(int32_t));
+    w.cnt = (int32_t*)take(2 * (size_t)idx.nlist * sizeof(int32_t));
+    w.off = (int32_t*)take(2 * (size_t)(idx.nlist + 1) * sizeof(int32_t));
+    w.cursor = (int32_t*)take(2 * (size_t)idx.nlist * sizeof(int32_t));
+    w.item_off = (int32_t*)take(2 * (size_t)(idx.nlist + 1) * sizeof(int32_t));
+    w.pair_q = (int32_t*)take(pairs * sizeof(int32_t));
+    w.pair_p = (int32_t*)take(pairs * sizeof(int32_t));
+    w.items = (int4*)take(pairs * sizeof(int4));
+    w.tau = (uint32_t*)take(Bs * sizeof(uint32_t));
+    w.cand_d = (float*)take(pairs * (size_t)K * sizeof(float));
+    w.cand_i = (int32_t*)take(pairs * (size_t)K * sizeof(int32_t));
+    w.ctr = (int32_t*)take(16 * sizeof(int32_t));
+    w.bytes = off;
+    if (ws) *ws = w;
+    return off;
+}
+
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+int trident_version(void) { return TRIDENT_ABI_VERSION; }
+
+const char* trident_last_error(void) { return g_err.c_str(); }
+
+int trident_index_check(const trident_index* idx) {
+    if (!idx) return fail(TRIDENT_ERR_INVALID, "index descriptor is NULL");
+    if (idx->D < 1 || idx->D > kMaxD) return fail(TRIDENT_ERR_UNSUPPORTED, "D=%d outside [1, %d]", idx->D, kMaxD);
+    if (idx->D_pad != ((idx->D + 31) / 32) * 32)
+        return fail(TRIDENT_ERR_INVALID, "D_pad=%d must be ceil(D/32)*32=%d", idx->D_pad, ((idx->D + 31) / 32) * 32);
+    if (idx->num_blocks != idx->D_pad / 32)
+        return fail(TRIDENT_ERR_INVALID, "num_blocks=%d must be D_pad/32=%d", idx->num_blocks, idx->D_pad / 32);
+    if (idx->nlist < 1) return fail(TRIDENT_ERR_INVALID, "nlist=%d", idx->nlist);
+    if (idx->tile_size != 128 && idx->tile_size != 256)
+        return fail(TRIDENT_ERR_UNSUPPORTED, "tile_size=%d (supported: 128, 256)", idx->tile_size);
+    if (idx->N < 0) return fail(TRIDENT_ERR_INVALID, "N=%lld", (long long)idx->N);
+    if (idx->N >= (int64_t)1 << 31) return fail(TRIDENT_ERR_UNSUPPORTED, "N=%lld exceeds int32 row ids", (long long)idx->N);
+    const void* ptrs[] = {idx->xb_sorted, idx->orig_ids_sorted, idx->list_row_off, idx->list_tile_off, idx->codes,
+                          idx->vmin, idx->delta, idx->eps, idx->centroids, idx->centroid_norm_sq,
+                          idx->pca_mean, idx->pca_rot};
+    const char* names[] = {"xb_sorted", "orig_ids_sorted", "list_row_off", "list_tile_off", "codes", "vmin",
+                           "delta", "eps", "centroids", "centroid_norm_sq", "pca_mean", "pca_rot"};
+    for (int i = 0; i < 12; ++i)
+        if (!ptrs[i]) return fail(TRIDENT_ERR_INVALID, "index array %s is NULL", names[i]);
+    if (((uintptr_t)idx->codes & 15) != 0) return fail(TRIDENT_ERR_INVALID, "codes must be 16-byte aligned");
+    if (!(idx->lb_rel_slack > 0.0f) || !(idx->centroid_norm_max >= 0.0f))
+        return fail(TRIDENT_ERR_INVALID, "lb_rel_slack / centroid_norm_max not set");
+    return TRIDENT_OK;
+}
+
+int trident_workspace_size(const trident_index* idx, int32_t B, int32_t K, int32_t nprobe, size_t* bytes) {
+    int rc = trident_index_check(idx);
+    if (rc) return rc;
+    if (!bytes) return fail(TRIDENT_ERR_INVALID, "bytes is NULL");
+    if (B < 0 || K < 1 || nprobe < 1) return fail(TRIDENT_ERR_INVALID, "B=%d K=%d nprobe=%d", B, K, nprobe);
+    *bytes = carve_workspace(*idx, B, K, nprobe, nullptr, nullptr);
+    return TRIDENT_OK;
+}
+
+int32_t trident_p_init(int32_t mode, int32_t B, int32_t K, int32_t nprobe) {
+    if (mode != TRIDENT_MODE_CASCADE) return 0;
+    if (nprobe <= 1) return 0;
+    if (B == 1 && K <= 10) return 1;
+    if (nprobe <= 16) return 2;
+    return 3;
+}
+
+int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, double w0) {
+    if (!idx || idx->nlist < 1) return TRIDENT_MODE_CASCADE;
+    if (!(w0 > 0.0)) w0 = 9.0e8;
+    const double W = (double)B * (double)nprobe * ((double)idx->N / (double)idx->nlist) * (double)idx->D;
+    return W < w0 ? TRIDENT_MODE_CM_FP32 : TRIDENT_MODE_CASCADE;
+}
+
+static int check_search_args(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
+                             void* workspace, size_t workspace_bytes, Workspace* ws) {
+    int rc = trident_index_check(idx);
+    if (rc) return rc;
+    if (B < 0) return fail(TRIDENT_ERR_INVALID, "B=%d", B);
+    if (K < 1 || K > kMaxK) return fail(TRIDENT_ERR_UNSUPPORTED, "K=%d outside [1, %d]", K, kMaxK);
+    if (nprobe < 1 || nprobe > idx->nlist || nprobe > kMaxNprobe)
+        return fail(TRIDENT_ERR_INVALID, "nprobe=%d outside [1, min(nlist=%d, %d)]", nprobe, idx->nlist, kMaxNprobe);
+    if (B > 0 && !xq) return fail(TRIDENT_ERR_INVALID, "xq is NULL");
+    if ((size_t)B * (size_t)nprobe >= ((size_t)1 << 31)) return fail(TRIDENT_ERR_UNSUPPORTED, "B*nprobe too large");
+    const size_t need = carve_workspace(*idx, B, K, nprobe, workspace, ws);
+    if (!workspace || workspace_bytes < need)
+        return fail(TRIDENT_ERR_WORKSPACE, "workspace of %zu bytes < %zu needed", workspace_bytes, need);
+    if (((uintptr_t)workspace & 255) != 0) return fail(TRIDENT_ERR_INVALID, "workspace must be 256-byte aligned");
+    return TRIDENT_OK;
+}
+
+#define TB_TRY(expr, where)                        \
+    do {                                           \
+        cudaError_t _e = (expr);                   \
+        if (_e != cudaSuccess) return cuda_fail(_e, where); \
+    } while (0)
+
+int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t nprobe, void* workspace,
+                   size_t workspace_bytes, int32_t* probe_cids, double* probe_d64, float* qrot, int64_t* stats,
+                   void* stream) {
+    Workspace ws;
+    int rc = check_search_args(idx, xq, B, 1, nprobe, workspace, workspace_bytes, &ws);
+    if (rc) return rc;
+    if (!probe_cids) return fail(TRIDENT_ERR_INVALID, "probe_cids is NULL");
+    if (B == 0) return TRIDENT_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, st), "coarse_gemm");
+    TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, probe_cids, probe_d64,
+                               (unsigned long long*)stats, st),
+           "probe_select");
+    g_launches += 3;
+    if (qrot)
+        TB_TRY(cudaMemcpyAsync(qrot, ws.qrot, (size_t)B * idx->D_pad * sizeof(float), cudaMemcpyDeviceToDevice, st),
+               "qrot copy");
+    return TRIDENT_OK;
+}
+
+// CUDA events around the phases of one search (profiled calls only).
+struct PhaseEvents {
+    cudaEvent_t ev[TRIDENT_PHASES + 1];
+    bool ran[TRIDENT_PHASES];
+    bool on = false;
+};
+
+static int search_impl(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, int32_t mode,
+                       int32_t ub_seed, void* workspace, size_t workspace_bytes, float* out_d, int64_t* out_i,
+                       int64_t* stats, cudaStream_t st, PhaseEvents* pe) {
+    Workspace ws;
+    int rc = check_search_args(idx, xq, B, K, nprobe, workspace, workspace_bytes, &ws);
+    if (rc) return rc;
+    if (B > 0 && (!out_d || !out_i)) return fail(TRIDENT_ERR_INVALID, "out_d / out_i is NULL");
+    if (ub_seed < 0 || ub_seed > 2) return fail(TRIDENT_ERR_INVALID, "ub_seed=%d outside [0, 2]", ub_seed);
+    if (mode == TRIDENT_MODE_AUTO) mode = trident_route(idx, B, nprobe, 0.0);
+    if (mode != TRIDENT_MODE_CASCADE && mode != TRIDENT_MODE_CM_FP32)
+        return fail(TRIDENT_ERR_UNSUPPORTED, "mode=%d (supported: -1 auto, 2 cascade, 10 CM-FP32)", mode);
+    if (B == 0) return TRIDENT_OK;
+    unsigned long long* sp = (unsigned long long*)stats;
+    const bool lb = mode == TRIDENT_MODE_CASCADE;
+    auto mark = [&](int phase) -> cudaError_t {  // event at the start of `phase` (or the end, PHASES)
+        if (!pe) return cudaSuccess;
+        if (phase < TRIDENT_PHASES) pe->ran[phase] = true;
+        return cudaEventRecord(pe->ev[phase], st);
+    };
+
+    TB_TRY(mark(TRIDENT_PHASE_COARSE), "event");
+    TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
+    TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, st), "coarse_gemm");
+    TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
+    g_launches += 3;
+
+    const int p_init = trident_p_init(mode, B, K, nprobe);
+    const int G = scan_group_size(*idx, K);
+    TB_TRY(mark(TRIDENT_PHASE_PAIRS), "event");
+    TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, p_init, G, K, ws, st), "pairs");
+    g_launches += 4;
+
+    ScanLaunch sl;
+    sl.K = K;
+    sl.nprobe = nprobe;
+    sl.G = G;
+    sl.lb = lb ? 1 : 0;
+    if (p_init > 0) {
+        sl.pass = 0;
+        sl.ub_seed = (lb && ub_seed >= 1) ? 1 : 0;
+        sl.max_items = B * p_init;
+        sl.item_base = 0;
+        TB_TRY(mark(TRIDENT_PHASE_SCAN0), "event");
+        TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan pass 0");
+        TB_TRY(mark(TRIDENT_PHASE_MERGE0), "event");
+        TB_TRY(launch_merge(ws, B, K, nprobe, 0, p_init, ws.tau, nullptr, nullptr, st), "merge pass 0");
+        g_launches += 2;
+    }
+    sl.pass = 1;
+    sl.ub_seed = (lb && (ub_seed == 2 || (ub_seed == 1 && p_init == 0))) ? 1 : 0;
+    sl.max_items = B * (nprobe - p_init);
+    sl.item_base = (int64_t)B * p_init;
+    TB_TRY(mark(TRIDENT_PHASE_SCAN1), "event");
+    TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan pass 1");
+    TB_TRY(mark(TRIDENT_PHASE_MERGE1), "event");
+    TB_TRY(launch_merge(ws, B, K, nprobe, 0, nprobe, nullptr, out_d, out_i, st), "merge");
+    g_launches += 2;
+    TB_TRY(mark(TRIDENT_PHASES), "event");
+    return TRIDENT_OK;
+}
+
+int trident_search(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, int32_t mode,
+                   int32_t ub_seed, void* workspace, size_t workspace_bytes, float* out_d, int64_t* out_i,
+                   int64_t* stats, void* stream) {
+    return search_impl(idx, xq, B, K, nprobe, mode, ub_seed, workspace, workspace_bytes, out_d, out_i, stats,
+                       (cudaStream_t)stream, nullptr);
+}
+
+int trident_search_profiled(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
+                            int32_t mode, int32_t ub_seed, void* workspace, size_t workspace_bytes, float* out_d,
+                            int64_t* out_i, int64_t* stats, void* stream, float* phase_ms) {
+    if (!phase_ms) return fail(TRIDENT_ERR_INVALID, "phase_ms is NULL");
+    cudaStream_t st = (cudaStream_t)stream;
+    PhaseEvents pe;
+    int created = 0;
+    for (; created <= TRIDENT_PHASES; ++created) {
+        if (cudaEventCreate(&pe.ev[created]) != cudaSuccess) break;
+    }
+    for (int i = 0; i < TRIDENT_PHASES; ++i) { pe.ran[i] = false; phase_ms[i] = 0.0f; }
+    int rc = TRIDENT_OK;
+    if (created <= TRIDENT_PHASES) {
+        rc = cuda_fail(cudaGetLastError(), "cudaEventCreate");
+    } else {
+        rc = search_impl(idx, xq, B, K, nprobe, mode, ub_seed, workspace, workspace_bytes, out_d, out_i, stats, st,
+                         &pe);
+        if (rc == TRIDENT_OK && B > 0) {
+            cudaError_t e = cudaEventSynchronize(pe.ev[TRIDENT_PHASES]);
+            if (e != cudaSuccess) rc = cuda_fail(e, "cudaEventSynchronize");
+            for (int i = 0; rc == TRIDENT_OK && i < TRIDENT_PHASES; ++i) {
+                if (!pe.ran[i]) continue;
+                int nxt = i + 1;
+                while (nxt < TRIDENT_PHASES && !pe.ran[nxt]) ++nxt;
+                float ms = 0.0f;
+                e = cudaEventElapsedTime(&ms, pe.ev[i], pe.ev[nxt]);
+                if (e != cudaSuccess) rc = cuda_fail(e, "cudaEventElapsedTime");
+                phase_ms[i] = ms;
+            }
+        }
+    }
+    for (int i = 0; i < created; ++i) cudaEventDestroy(pe.ev[i]);
+    return rc;
+}
+
+int64_t trident_launch_count(void) { return g_launches; }
+
+int trident_merge_shards(const float* d_in, const int64_t* i_in, int32_t R, int32_t B, int32_t K, float* out_d,
+                         int64_t* out_i, void* stream) {
+    if (R < 1 || B < 0 || K < 1 || K > kMaxK) return fail(TRIDENT_ERR_INVALID, "R=%d B=%d K=%d", R, B, K);
+    if (B == 0) return TRIDENT_OK;
+    if (!d_in || !i_in || !out_d || !out_i) return fail(TRIDENT_ERR_INVALID, "NULL buffer");
+    TB_TRY(launch_merge_shards(d_in, i_in, R, B, K, out_d, out_i, (cudaStream_t)stream), "merge_shards");
+    return TRIDENT_OK;
+}
+
+}  // extern "C"

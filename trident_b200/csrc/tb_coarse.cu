@@ -1,0 +1,337 @@
+// Coarse stage of the query path: PCA rotation of the queries and exact top-nprobe list selection.
+//
+// The reference runs one cuBLAS FP32 GEMM for both (proj = xq [-2C^T | R] + [||c||^2 | -muR],
+// src/trident_v4_kernels.cu:1233-1246) and then selects the nprobe smallest coarse distances per
+// query with nprobe rounds of block argmin over an smem copy of the row (:68-162), which cannot
+// launch once 4*nlist bytes exceed the smem limit (nlist >~ 58k).
+//
+// Here:
+//  * the rotation runs in float64 (DFMA) and is rounded once to float32, so the rotated query that
+//    the Stage-Y bound uses is within half an ulp of (q - mu)R; its norm bound sigma feeds the
+//    bound's slack;
+//  * the coarse distances are computed approximately (a GEMM with a certified error bound E), a
+//    radix select finds the nprobe-th approximate value t, and every list whose approximate value
+//    is within t + 2E (+ float64 slack) is re-checked with the exact float64 ||q - c||^2. The exact
+//    values are sorted by (distance, list id), so the probe set and its order are exactly the
+//    oracle's (ties to the smaller list id, as :122/:131), whatever the GEMM's rounding.
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "tb_common.cuh"
+#include "tb_internal.h"
+
+namespace tb {
+
+// ------------------------------------------------------------------------------------------
+// Rotation: qrot[j][d] = float((q_j - mu) R[:, d]) with k ascending and fma (the oracle's
+// oracle_rotate_f64). QT queries per block share each R column read; thread = output dim.
+// Block-column 0 also writes the per-query norms and resets the query's threshold to +inf.
+// ------------------------------------------------------------------------------------------
+constexpr int kRotThreads = 256;
+constexpr int kRotMaxQT = 8;
+
+__global__ void __launch_bounds__(kRotThreads) rotate_f64_kernel(
+    const float* __restrict__ xq, const double* __restrict__ mu, const double* __restrict__ R, int B, int D,
+    int D_pad, int QT, float* __restrict__ qrot, float* __restrict__ qinfo, uint32_t* __restrict__ tau) {
+    extern __shared__ double qm[];  // [QT][D]
+    __shared__ double red[2][kRotThreads / 32];
+    const int j0 = blockIdx.x * QT;
+    const int nq = min(QT, B - j0);
+    const int tid = threadIdx.x;
+    for (int i = tid; i < nq * D; i += blockDim.x) {
+        const int j = i / D, k = i - j * D;
+        qm[i] = (double)xq[(int64_t)(j0 + j) * D + k] - mu[k];
+    }
+    __syncthreads();
+    const int d = blockIdx.y * blockDim.x + tid;
+    if (d < D_pad) {
+        double acc[kRotMaxQT];
+#pragma unroll
+        for (int j = 0; j < kRotMaxQT; ++j) acc[j] = 0.0;
+        if (d < D) {
+            for (int k = 0; k < D; ++k) {
+                const double r = __ldg(R + (int64_t)k * D + d);
+#pragma unroll
+                for (int j = 0; j < kRotMaxQT; ++j)
+                    if (j < nq) acc[j] = fma(qm[j * D + k], r, acc[j]);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kRotMaxQT; ++j)
+            if (j < nq) qrot[(int64_t)(j0 + j) * D_pad + d] = (float)acc[j];
+    }
+    if (blockIdx.y == 0) {
+        const int lane = tid & 31, warp = tid >> 5;
+        for (int j = 0; j < nq; ++j) {
+            double s_q = 0.0, s_c = 0.0;
+            for (int k = tid; k < D; k += blockDim.x) {
+                const double v = (double)xq[(int64_t)(j0 + j) * D + k];
+                s_q = fma(v, v, s_q);
+                s_c = fma(qm[j * D + k], qm[j * D + k], s_c);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                s_q += __shfl_xor_sync(TB_FULL, s_q, o);
+                s_c += __shfl_xor_sync(TB_FULL, s_c, o);
+            }
+            if (lane == 0) { red[0][warp] = s_q; red[1][warp] = s_c; }
+            __syncthreads();
+            if (tid == 0) {
+                double tq = 0.0, tc = 0.0;
+                for (int w = 0; w < (int)(blockDim.x / 32); ++w) { tq += red[0][w]; tc += red[1][w]; }
+                const double qn = sqrt(tq) * (1.0 + 1e-12);
+                const double cn = sqrt(tc) * (1.0 + 1e-12);
+                // sigma: Minkowski slack for the query-side float32 roundings of the bound
+                // (3u|q~_d| per dim) plus the float64 rotation error per dim.
+                const double u = 5.9604644775390625e-08;  // 2^-24
+                const double sigma = (3.0001 * u * cn + sqrt((double)D_pad) * (D + 2) * 2.220446049250313e-16 * cn) *
+                                     (1.0 + 1e-6);
+                float* qi = qinfo + (int64_t)(j0 + j) * QI_LEN;
+                qi[QI_QNORM] = __double2float_ru(qn);
+                qi[QI_SIGMA] = __double2float_ru(sigma);
+                qi[QI_CNORM] = __double2float_ru(cn);
+                qi[QI_PAD] = 0.0f;
+                tau[j0 + j] = __float_as_uint(kInf);
+            }
+            __syncthreads();
+        }
+    }
+}
+
+cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
+                          uint32_t* tau, cudaStream_t st) {
+    int QT = 12288 / idx.D;
+    QT = QT < 1 ? 1 : (QT > kRotMaxQT ? kRotMaxQT : QT);
+    const size_t smem = (size_t)QT * idx.D * sizeof(double);
+    if (smem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(rotate_f64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    dim3 grid((B + QT - 1) / QT, (idx.D_pad + kRotThreads - 1) / kRotThreads);
+    rotate_f64_kernel<<<grid, kRotThreads, smem, st>>>(xq, idx.pca_mean, idx.pca_rot, B, idx.D, idx.D_pad, QT, qrot,
+                                                      qinfo, tau);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------
+// Approximate coarse distances a[j][c] = ||c||^2 - 2 q_j.c (float32 SIMT GEMM, 64x64 tiles).
+// Any summation order satisfies the bound the selection uses: |a - exact| <= (D+2) u
+// (2||q|| Cmax + Cmax^2).
+// ------------------------------------------------------------------------------------------
+constexpr int kGM = 64, kGN = 64, kGK = 16;
+
+__global__ void __launch_bounds__(256) coarse_gemm_kernel(const float* __restrict__ xq, const float* __restrict__ cent,
+                                                         const float* __restrict__ cn, int B, int nlist, int D,
+                                                         float* __restrict__ out) {
+    __shared__ float sA[kGK][kGM + 4];
+    __shared__ float sB[kGK][kGN + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * kGM, n0 = blockIdx.x * kGN;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < D; k0 += kGK) {
+        for (int i = threadIdx.x; i < kGM * kGK; i += 256) {
+            const int r = i / kGK, k = i - r * kGK;
+            const int gm = m0 + r, gk = k0 + k;
+            sA[k][r] = (gm < B && gk < D) ? __ldg(xq + (int64_t)gm * D + gk) : 0.0f;
+            const int gn = n0 + r;
+            sB[k][r] = (gn < nlist && gk < D) ? __ldg(cent + (int64_t)gn * D + gk) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kGK; ++k) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { a[i] = sA[k][ty * 4 + i]; b[i] = sB[k][tx * 4 + i]; }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int gm = m0 + ty * 4 + i;
+        if (gm >= B) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gn = n0 + tx * 4 + j;
+            if (gn < nlist) out[(int64_t)gm * nlist + gn] = cn[gn] - 2.0f * acc[i][j];
+        }
+    }
+}
+
+cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, cudaStream_t st) {
+    dim3 grid((idx.nlist + kGN - 1) / kGN, (B + kGM - 1) / kGM);
+    coarse_gemm_kernel<<<grid, 256, 0, st>>>(xq, idx.centroids, idx.centroid_norm_sq, B, idx.nlist, idx.D, coarse);
+    return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------------------
+// Exact top-nprobe selection, one CTA per query.
+// ------------------------------------------------------------------------------------------
+constexpr int kSelThreads = 512;
+constexpr int kSelCap = 2048;  // sorted best (<= nprobe <= 1024) + one batch of re-check members
+
+__device__ void bitonic_sort_kc(unsigned long long* key, int32_t* cid, int P) {
+    for (int k = 2; k <= P; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const bool up = (i & k) == 0;
+                    const unsigned long long a = key[i], b = key[ixj];
+                    const int32_t ca = cid[i], cb = cid[ixj];
+                    const bool gt = (a > b) || (a == b && ca > cb);
+                    if (gt == up) {
+                        key[i] = b; key[ixj] = a;
+                        cid[i] = cb; cid[ixj] = ca;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
+    const float* __restrict__ coarse, const float* __restrict__ xq, const float* __restrict__ cent,
+    const float* __restrict__ qinfo, int nlist, int D, int nprobe, float cmax, int32_t* __restrict__ probe,
+    double* __restrict__ probe_d64, unsigned long long* __restrict__ stats) {
+    extern __shared__ float qv[];  // [D]
+    __shared__ unsigned long long skey[kSelCap];
+    __shared__ int32_t scid[kSelCap];
+    __shared__ uint32_t hist[256];
+    __shared__ uint32_t s_bucket, s_k;
+    __shared__ int s_batch;
+    const int j = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* row = coarse + (int64_t)j * nlist;
+    for (int d = tid; d < D; d += blockDim.x) qv[d] = xq[(int64_t)j * D + d];
+
+    // 1) radix select of the nprobe-th smallest approximate value (4 x 8-bit digits)
+    uint32_t prefix = 0, pmask = 0;
+    uint32_t kk = (uint32_t)nprobe;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
+        __syncthreads();
+        for (int c = tid; c < nlist; c += blockDim.x) {
+            const uint32_t key = float_key(__ldg(row + c));
+            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t h[8], s = 0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) { h[i] = hist[lane * 8 + i]; s += h[i]; }
+            uint32_t incl = s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t n = __shfl_up_sync(TB_FULL, incl, o);
+                if (lane >= o) incl += n;
+            }
+            const uint32_t excl = incl - s;
+            if (excl < kk && kk <= incl) {
+                uint32_t cum = excl;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    if (cum + h[i] >= kk) { s_bucket = lane * 8 + i; s_k = kk - cum; break; }
+                    cum += h[i];
+                }
+            }
+        }
+        __syncthreads();
+        prefix |= s_bucket << shift;
+        pmask |= 0xFFu << shift;
+        kk = s_k;
+        __syncthreads();
+    }
+    const float t = key_float(prefix);
+
+    // 2) members: approximate value within the certified band above t
+    const double u = 5.9604644775390625e-08;
+    const float* qi = qinfo + (int64_t)j * QI_LEN;
+    const double qn = (double)qi[QI_QNORM];
+    const double cm = (double)cmax;
+    const double E = (double)(D + 4) * u * 1.01 * (2.0 * qn * cm + cm * cm);
+    const double eta = (double)(D + 2) * 2.220446049250313e-16 * (qn + cm) * (qn + cm);
+    const float thr = __double2float_ru((double)t + 2.0 * E + 2.0 * eta);
+
+    int best_n = 0;
+    int batch = 0;
+    if (tid == 0) s_batch = 0;
+    __syncthreads();
+    long long members = 0;
+    auto process_batch = [&]() {
+        // exact float64 distance of each batch member, then sort best + batch by (d64, cid)
+        for (int i = tid; i < batch; i += blockDim.x) {
+            const int c = scid[best_n + i];
+            const float* cr = cent + (int64_t)c * D;
+            double acc = 0.0;
+            for (int d = 0; d < D; ++d) {
+                const double df = (double)qv[d] - (double)__ldg(cr + d);
+                acc = fma(df, df, acc);
+            }
+            skey[best_n + i] = (unsigned long long)__double_as_longlong(acc);
+        }
+        const int n = best_n + batch;
+        int P = 1;
+        while (P < n) P <<= 1;
+        for (int i = n + tid; i < P; i += blockDim.x) { skey[i] = ~0ull; scid[i] = 0x7fffffff; }
+        __syncthreads();
+        bitonic_sort_kc(skey, scid, P);
+        best_n = n < nprobe ? n : nprobe;
+        batch = 0;
+        if (tid == 0) s_batch = 0;
+        __syncthreads();
+    };
+    for (int cs = 0; cs < nlist; cs += blockDim.x) {
+        const int c = cs + tid;
+        const bool mem = (c < nlist) && (__ldg(row + c) <= thr);
+        const int chunk = __syncthreads_count(mem);
+        if (chunk == 0) continue;
+        members += chunk;
+        if (best_n + batch + chunk > kSelCap) process_batch();
+        const unsigned m = __ballot_sync(TB_FULL, mem);
+        if (m) {
+            const int leader = __ffs(m) - 1;
+            int pos = 0;
+            if (lane == leader) pos = atomicAdd(&s_batch, __popc(m));
+            pos = __shfl_sync(TB_FULL, pos, leader);
+            if (mem) scid[best_n + pos + __popc(m & ((1u << lane) - 1u))] = c;
+        }
+        __syncthreads();
+        batch = s_batch;
+        __syncthreads();
+    }
+    if (batch > 0) process_batch();
+    // best_n >= nprobe whenever the row is finite; a non-finite query leaves the tail as -1
+    // (skipped by the pair kernels, whose candidate slots then stay empty).
+    for (int p = tid; p < nprobe; p += blockDim.x) {
+        const bool ok = p < best_n;
+        probe[(int64_t)j * nprobe + p] = ok ? scid[p] : -1;
+        if (probe_d64) probe_d64[(int64_t)j * nprobe + p] = ok ? __longlong_as_double((long long)skey[p]) : kInf;
+    }
+    if (stats && tid == 0) atomicAdd(stats + TRIDENT_STAT_COARSE_RECHECK, (unsigned long long)members);
+}
+
+cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B, int nprobe, const float* coarse,
+                                const float* qinfo, int32_t* probe, double* probe_d64, unsigned long long* stats,
+                                cudaStream_t st) {
+    const size_t smem = (size_t)idx.D * sizeof(float);
+    if (smem > 16 * 1024) {
+        cudaError_t e =
+            cudaFuncSetAttribute(probe_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+    }
+    probe_select_kernel<<<B, kSelThreads, smem, st>>>(coarse, xq, idx.centroids, qinfo, idx.nlist, idx.D, nprobe,
+                                                      idx.centroid_norm_max, probe, probe_d64, stats);
+    return cudaGetLastError();
+}
+
+}  // namespace tb

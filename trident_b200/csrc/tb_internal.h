@@ -1,0 +1,70 @@
+// Host-side launchers shared between the trident_b200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "trident_b200.h"
+
+namespace tb {
+
+// Per-query side information written by the rotation kernel.
+enum QInfo { QI_QNORM = 0, QI_SIGMA = 1, QI_CNORM = 2, QI_PAD = 3, QI_LEN = 4 };
+
+// Workspace carve-up for one call (B, K, nprobe); every region is 256-byte aligned.
+struct Workspace {
+    float* qrot;        // [B, D_pad]
+    float* qinfo;       // [B, QI_LEN]
+    float* coarse;      // [B, nlist] approximate ||c||^2 - 2 q.c
+    int32_t* probe;     // [B, nprobe]
+    int32_t* cnt;       // [2, nlist]
+    int32_t* off;       // [2, nlist + 1]
+    int32_t* cursor;    // [2, nlist]
+    int32_t* item_off;  // [2, nlist + 1]
+    int32_t* pair_q;    // [B * nprobe]
+    int32_t* pair_p;    // [B * nprobe]
+    int4* items;        // [B * nprobe]
+    uint32_t* tau;      // [B] float bits of each query's current K-th distance
+    float* cand_d;      // [B, nprobe, K]
+    int32_t* cand_i;    // [B, nprobe, K]
+    int32_t* ctr;       // [16] item counts and work counters
+    size_t bytes;
+};
+
+size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void* base, Workspace* ws);
+
+// Coarse stage (tb_coarse.cu).
+cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
+                          uint32_t* tau, cudaStream_t st);
+cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, cudaStream_t st);
+cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B, int nprobe, const float* coarse,
+                                const float* qinfo, int32_t* probe, double* probe_d64,
+                                unsigned long long* stats, cudaStream_t st);
+
+// Pair lists and work items (tb_pairs.cu).
+cudaError_t launch_pairs(const trident_index& idx, const int32_t* probe, int B, int nprobe, int p_init, int G, int K,
+                         const Workspace& ws, cudaStream_t st);
+
+// Scans and merges (tb_scan.cu).
+struct ScanLaunch {
+    int pass;        // 0: warm-up lists, 1: the rest
+    int K;
+    int nprobe;
+    int G;           // queries per work item
+    int lb;          // 1: Stage Y lower bound (cascade), 0: CM-FP32 exact scan
+    int ub_seed;     // 1: seed each item's threshold from SQ8 upper bounds first
+    int max_items;   // upper bound on the item count of this pass
+    int64_t item_base;  // index of this pass's first item in the item array
+};
+cudaError_t launch_scan(const trident_index& idx, const float* xq, const Workspace& ws, const ScanLaunch& sl,
+                        unsigned long long* stats, cudaStream_t st);
+int scan_group_size(const trident_index& idx, int K);
+cudaError_t launch_merge(const Workspace& ws, int B, int K, int nprobe, int p_lo, int p_hi, uint32_t* tau_out,
+                         float* out_d, int64_t* out_i, cudaStream_t st);
+cudaError_t launch_merge_shards(const float* d_in, const int64_t* i_in, int R, int B, int K, float* out_d,
+                                int64_t* out_i, cudaStream_t st);
+
+int num_sms();
+
+}  // namespace tb

@@ -1,0 +1,145 @@
+// Cluster-major work lists: (list, query) pairs grouped by list, then split into work items of at
+// most G queries.
+//
+// The reference sorts (cid, qid, dqc) pairs of each pass with one 256-thread CTA per pass and an
+// smem histogram of nlist+1 counters (src/trident_v4_kernels.cu:168-263), which serialises 2.5-5M
+// pairs at the large configs and cannot launch for nlist >~ 58k. Here the histogram and scatter run
+// over the whole GPU with global atomics, one 1024-thread CTA per pass scans the counts, and a
+// final kernel emits the items. Pass 0 holds probes p < p_init (the warm-up lists), pass 1 the rest.
+// The order of queries inside a list is not deterministic; results do not depend on it.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "tb_common.cuh"
+#include "tb_internal.h"
+
+namespace tb {
+
+__global__ void pair_hist_kernel(const int32_t* __restrict__ probe, int64_t total, int nprobe, int p_init, int nlist,
+                                 int32_t* __restrict__ cnt) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i % nprobe);
+        const int s = p >= p_init;
+        const int32_t c = probe[i];
+        if ((unsigned)c < (unsigned)nlist) atomicAdd(&cnt[s * nlist + c], 1);
+    }
+}
+
+// One CTA per pass: exclusive scans of the pair counts and of the per-list item counts
+// ceil(cnt / G); cursors start at the pair offsets; ctr[pass] receives the item count.
+__global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t* __restrict__ cnt, int nlist, int G,
+                                                        int32_t* __restrict__ off, int32_t* __restrict__ item_off,
+                                                        int32_t* __restrict__ cursor, int32_t* __restrict__ ctr) {
+    __shared__ int32_t wsum[2][32];
+    const int s = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int32_t* c_in = cnt + (int64_t)s * nlist;
+    int32_t* o = off + (int64_t)s * (nlist + 1);
+    int32_t* io = item_off + (int64_t)s * (nlist + 1);
+    int32_t* cur = cursor + (int64_t)s * nlist;
+    int32_t run_p = 0, run_i = 0;
+    for (int base = 0; base < nlist; base += 1024) {
+        const int c = base + tid;
+        const int32_t vp = (c < nlist) ? c_in[c] : 0;
+        const int32_t vi = (vp + G - 1) / G;
+        int32_t sp = vp, si = vi;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int32_t np = __shfl_up_sync(TB_FULL, sp, d);
+            const int32_t ni = __shfl_up_sync(TB_FULL, si, d);
+            if (lane >= d) { sp += np; si += ni; }
+        }
+        if (lane == 31) { wsum[0][warp] = sp; wsum[1][warp] = si; }
+        __syncthreads();
+        if (warp == 0) {
+            int32_t wp = wsum[0][lane], wi = wsum[1][lane];
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int32_t np = __shfl_up_sync(TB_FULL, wp, d);
+                const int32_t ni = __shfl_up_sync(TB_FULL, wi, d);
+                if (lane >= d) { wp += np; wi += ni; }
+            }
+            wsum[0][lane] = wp;
+            wsum[1][lane] = wi;
+        }
+        __syncthreads();
+        const int32_t pre_p = (warp > 0 ? wsum[0][warp - 1] : 0) + sp - vp;
+        const int32_t pre_i = (warp > 0 ? wsum[1][warp - 1] : 0) + si - vi;
+        if (c < nlist) {
+            o[c] = run_p + pre_p;
+            cur[c] = run_p + pre_p;
+            io[c] = run_i + pre_i;
+        }
+        run_p += wsum[0][31];
+        run_i += wsum[1][31];
+        __syncthreads();
+    }
+    if (tid == 0) {
+        o[nlist] = run_p;
+        io[nlist] = run_i;
+        ctr[s] = run_i;
+    }
+}
+
+__global__ void pair_scatter_kernel(const int32_t* __restrict__ probe, int64_t total, int nprobe, int p_init,
+                                    int nlist, int64_t base1, int32_t* __restrict__ cursor,
+                                    int32_t* __restrict__ pair_q, int32_t* __restrict__ pair_p, int K,
+                                    float* __restrict__ cand_d, int32_t* __restrict__ cand_i) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int p = (int)(i % nprobe);
+        const int q = (int)(i / nprobe);
+        const int s = p >= p_init;
+        const int32_t c = probe[i];
+        if ((unsigned)c >= (unsigned)nlist) {  // no list for this probe: its slots stay empty
+            for (int k = 0; k < K; ++k) {
+                cand_d[i * K + k] = kInf;
+                cand_i[i * K + k] = -1;
+            }
+            continue;
+        }
+        const int64_t pos = (s ? base1 : 0) + atomicAdd(&cursor[s * nlist + c], 1);
+        pair_q[pos] = q;
+        pair_p[pos] = p;
+    }
+}
+
+// Items (list, first pair, query count) in list order; pass 1's items start at items + base1.
+__global__ void item_emit_kernel(const int32_t* __restrict__ cnt, const int32_t* __restrict__ off,
+                                 const int32_t* __restrict__ item_off, int nlist, int G, int64_t base1,
+                                 int4* __restrict__ items) {
+    const int s = blockIdx.y;
+    for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < nlist; c += gridDim.x * blockDim.x) {
+        const int32_t n = cnt[s * nlist + c];
+        if (n == 0) continue;
+        const int32_t po = off[s * (nlist + 1) + c];
+        const int32_t io = item_off[s * (nlist + 1) + c];
+        int4* dst = items + (s ? base1 : 0) + io;
+        for (int g = 0; g * G < n; ++g) {
+            const int32_t m = min(G, n - g * G);
+            dst[g] = make_int4(c, (int)((s ? base1 : 0) + po + g * G), m, 0);
+        }
+    }
+}
+
+cudaError_t launch_pairs(const trident_index& idx, const int32_t* probe, int B, int nprobe, int p_init, int G, int K,
+                         const Workspace& ws, cudaStream_t st) {
+    const int nlist = idx.nlist;
+    const int64_t total = (int64_t)B * nprobe;
+    const int64_t base1 = (int64_t)B * p_init;
+    cudaError_t e = cudaMemsetAsync(ws.cnt, 0, sizeof(int32_t) * 2 * (size_t)nlist, st);
+    if (e != cudaSuccess) return e;
+    const int threads = 256;
+    int blocks = (int)((total + threads - 1) / threads);
+    const int cap = num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    pair_hist_kernel<<<blocks, threads, 0, st>>>(probe, total, nprobe, p_init, nlist, ws.cnt);
+    pair_scan_kernel<<<2, 1024, 0, st>>>(ws.cnt, nlist, G, ws.off, ws.item_off, ws.cursor, ws.ctr);
+    pair_scatter_kernel<<<blocks, threads, 0, st>>>(probe, total, nprobe, p_init, nlist, base1, ws.cursor, ws.pair_q,
+                                                     ws.pair_p, K, ws.cand_d, ws.cand_i);
+    dim3 g2((nlist + 255) / 256, 2);
+    item_emit_kernel<<<g2, 256, 0, st>>>(ws.cnt, ws.off, ws.item_off, nlist, G, base1, ws.items);
+    return cudaGetLastError();
+}
+
+}  // namespace tb
