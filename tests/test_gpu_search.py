@@ -94,13 +94,21 @@ def test_small_batches_and_warmup_splits(cases, B, nprobe):
         assert_same_topk(d, i, od, oi)
 
 
-def test_fewer_rows_than_k(cases):
-    """K = 100 from one small list: missing slots come back as (+inf, -1)."""
-    f = cases["g4_ties"]
-    od, oi, _ = _oracle(f, nprobe=1, K=100)
-    d, i = _search(f["index"], f["xq"], 1, 100, mode=2)
-    assert_same_topk(d, i, od, oi)
-    assert (i == -1).any() and np.isinf(d[i == -1]).all()
+def test_fewer_rows_than_k():
+    """K = 100 from lists of a few rows: missing slots come back as (+inf, -1)."""
+    rng = np.random.default_rng(1)
+    D, sizes = 64, [3, 5, 0, 7, 40]
+    cent = rng.standard_normal((len(sizes), D)).astype(np.float32) * 4
+    xb = np.concatenate([cent[c] + rng.standard_normal((n, D)).astype(np.float32) for c, n in enumerate(sizes)])
+    lids = np.repeat(np.arange(len(sizes)), sizes).astype(np.int32)
+    xq = (cent[rng.integers(0, len(sizes), 30)] + rng.standard_normal((30, D))).astype(np.float32)
+    idx = _custom_index(xb, cent, lids, D)
+    for nprobe in (1, 2):
+        od, oi, _ = oracle_search(xb, lids, cent, xq, nprobe, 100)
+        for mode in (2, 10):
+            d, i = _search(idx, xq, nprobe, 100, mode=mode)
+            assert_same_topk(d, i, od, oi)
+            assert (i == -1).any() and np.isinf(d[i == -1]).all()
 
 
 def _custom_index(xb, cent, list_ids, D):
@@ -231,3 +239,14 @@ def test_config_parity(cfg_name, overrides, modes):
     for mode in modes:
         d, i = _search(idx, xq, cfg.nprobe, cfg.K, mode=mode)
         assert_same_topk(d, i, od, oi)
+
+
+def test_repeated_searches_are_identical_to_the_oracle(cases):
+    """Thresholds are exchanged between CTAs through atomics, so pruning differs from run to run;
+    the results must not. Repeat the same searches and compare every run with the oracle."""
+    for name, K in (("g3_norm_c3", 10), ("g3_norm_c3", 50), ("g2_decay_c2", 10)):
+        f = cases[name]
+        od, oi, _ = _oracle(f, K=K)
+        for _ in range(5):
+            d, i = _search(f["index"], f["xq"], int(f["nprobe"]), K, mode=2)
+            assert_same_topk(d, i, od, oi)

@@ -185,7 +185,7 @@ int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, probe_cids, probe_d64,
                                (unsigned long long*)stats, st),
            "probe_select");
-    g_launches += 3;
+    g_launches += 4;
     if (qrot)
         TB_TRY(cudaMemcpyAsync(qrot, ws.qrot, (size_t)B * idx->D_pad * sizeof(float), cudaMemcpyDeviceToDevice, st),
                "qrot copy");
@@ -224,7 +224,7 @@ static int search_impl(const trident_index* idx, const float* xq, int32_t B, int
     TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
     TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, st), "coarse_gemm");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
-    g_launches += 3;
+    g_launches += 4;
 
     const int p_init = trident_p_init(mode, B, K, nprobe);
     const int G = scan_group_size(*idx, K);

@@ -25,92 +25,102 @@ namespace tb {
 
 // ------------------------------------------------------------------------------------------
 // Rotation: qrot[j][d] = float((q_j - mu) R[:, d]) with k ascending and fma (the oracle's
-// oracle_rotate_f64). QT queries per block share each R column read; thread = output dim.
-// Block-column 0 also writes the per-query norms and resets the query's threshold to +inf.
+// oracle_rotate_f64), as a register-tiled float64 GEMM: 64 queries x 64 dims per CTA, 16-deep
+// k-slices staged in shared memory, 4 x 4 outputs per thread. The k order of every output stays
+// sequential, so the result is bit-identical to the oracle.
 // ------------------------------------------------------------------------------------------
-constexpr int kRotThreads = 256;
-constexpr int kRotMaxQT = 8;
+constexpr int kRM = 64, kRN = 64, kRK = 16;
 
-__global__ void __launch_bounds__(kRotThreads) rotate_f64_kernel(
-    const float* __restrict__ xq, const double* __restrict__ mu, const double* __restrict__ R, int B, int D,
-    int D_pad, int QT, float* __restrict__ qrot, float* __restrict__ qinfo, uint32_t* __restrict__ tau) {
-    extern __shared__ double qm[];  // [QT][D]
-    __shared__ double red[2][kRotThreads / 32];
-    const int j0 = blockIdx.x * QT;
-    const int nq = min(QT, B - j0);
-    const int tid = threadIdx.x;
-    for (int i = tid; i < nq * D; i += blockDim.x) {
-        const int j = i / D, k = i - j * D;
-        qm[i] = (double)xq[(int64_t)(j0 + j) * D + k] - mu[k];
-    }
-    __syncthreads();
-    const int d = blockIdx.y * blockDim.x + tid;
-    if (d < D_pad) {
-        double acc[kRotMaxQT];
+__global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict__ xq, const double* __restrict__ mu,
+                                                        const double* __restrict__ R, int B, int D, int D_pad,
+                                                        float* __restrict__ qrot) {
+    __shared__ double sQ[kRK][kRM + 1];
+    __shared__ double sR[kRK][kRN + 1];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.x * kRM, n0 = blockIdx.y * kRN;
+    double acc[4][4];
 #pragma unroll
-        for (int j = 0; j < kRotMaxQT; ++j) acc[j] = 0.0;
-        if (d < D) {
-            for (int k = 0; k < D; ++k) {
-                const double r = __ldg(R + (int64_t)k * D + d);
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < kRotMaxQT; ++j)
-                    if (j < nq) acc[j] = fma(qm[j * D + k], r, acc[j]);
-            }
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+    for (int k0 = 0; k0 < D; k0 += kRK) {
+        const int kn = min(kRK, D - k0);
+        for (int i = threadIdx.x; i < kRM * kRK; i += 256) {
+            const int r = i / kRK, k = i - r * kRK;
+            const int gm = m0 + r, gk = k0 + k;
+            sQ[k][r] = (gm < B && k < kn) ? (double)__ldg(xq + (int64_t)gm * D + gk) - __ldg(mu + gk) : 0.0;
         }
-#pragma unroll
-        for (int j = 0; j < kRotMaxQT; ++j)
-            if (j < nq) qrot[(int64_t)(j0 + j) * D_pad + d] = (float)acc[j];
-    }
-    if (blockIdx.y == 0) {
-        const int lane = tid & 31, warp = tid >> 5;
-        for (int j = 0; j < nq; ++j) {
-            double s_q = 0.0, s_c = 0.0;
-            for (int k = tid; k < D; k += blockDim.x) {
-                const double v = (double)xq[(int64_t)(j0 + j) * D + k];
-                s_q = fma(v, v, s_q);
-                s_c = fma(qm[j * D + k], qm[j * D + k], s_c);
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                s_q += __shfl_xor_sync(TB_FULL, s_q, o);
-                s_c += __shfl_xor_sync(TB_FULL, s_c, o);
-            }
-            if (lane == 0) { red[0][warp] = s_q; red[1][warp] = s_c; }
-            __syncthreads();
-            if (tid == 0) {
-                double tq = 0.0, tc = 0.0;
-                for (int w = 0; w < (int)(blockDim.x / 32); ++w) { tq += red[0][w]; tc += red[1][w]; }
-                const double qn = sqrt(tq) * (1.0 + 1e-12);
-                const double cn = sqrt(tc) * (1.0 + 1e-12);
-                // sigma: Minkowski slack for the query-side float32 roundings of the bound
-                // (3u|q~_d| per dim) plus the float64 rotation error per dim.
-                const double u = 5.9604644775390625e-08;  // 2^-24
-                const double sigma = (3.0001 * u * cn + sqrt((double)D_pad) * (D + 2) * 2.220446049250313e-16 * cn) *
-                                     (1.0 + 1e-6);
-                float* qi = qinfo + (int64_t)(j0 + j) * QI_LEN;
-                qi[QI_QNORM] = __double2float_ru(qn);
-                qi[QI_SIGMA] = __double2float_ru(sigma);
-                qi[QI_CNORM] = __double2float_ru(cn);
-                qi[QI_PAD] = 0.0f;
-                tau[j0 + j] = __float_as_uint(kInf);
-            }
-            __syncthreads();
+        for (int i = threadIdx.x; i < kRK * kRN; i += 256) {
+            const int k = i / kRN, n = i - k * kRN;
+            const int gn = n0 + n;
+            sR[k][n] = (k < kn && gn < D) ? __ldg(R + (int64_t)(k0 + k) * D + gn) : 0.0;
         }
+        __syncthreads();
+        for (int k = 0; k < kn; ++k) {
+            double a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) { a[i] = sQ[k][ty * 4 + i]; b[i] = sR[k][tx * 4 + i]; }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int gm = m0 + ty * 4 + i;
+        if (gm >= B) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gn = n0 + tx * 4 + j;
+            if (gn < D_pad) qrot[(int64_t)gm * D_pad + gn] = gn < D ? (float)acc[i][j] : 0.0f;
+        }
+    }
+}
+
+// Per-query norms (one warp per query): ||q|| for the coarse bound, ||q - mu|| for sigma; the
+// query's threshold starts at +inf.
+__global__ void __launch_bounds__(256) query_norms_kernel(const float* __restrict__ xq, const double* __restrict__ mu,
+                                                         int B, int D, int D_pad, float* __restrict__ qinfo,
+                                                         uint32_t* __restrict__ tau) {
+    const int lane = threadIdx.x & 31;
+    const int j = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (j >= B) return;
+    double s_q = 0.0, s_c = 0.0;
+    for (int k = lane; k < D; k += 32) {
+        const double v = (double)xq[(int64_t)j * D + k];
+        const double w = v - mu[k];
+        s_q = fma(v, v, s_q);
+        s_c = fma(w, w, s_c);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        s_q += __shfl_xor_sync(TB_FULL, s_q, o);
+        s_c += __shfl_xor_sync(TB_FULL, s_c, o);
+    }
+    if (lane == 0) {
+        const double qn = sqrt(s_q) * (1.0 + 1e-12);
+        const double cn = sqrt(s_c) * (1.0 + 1e-12);
+        // sigma: Minkowski slack for the query-side float32 roundings of the bound (3u|q~_d| per
+        // dim) plus the float64 rotation error per dim.
+        const double u = 5.9604644775390625e-08;  // 2^-24
+        const double sigma =
+            (3.0001 * u * cn + sqrt((double)D_pad) * (D + 2) * 2.220446049250313e-16 * cn) * (1.0 + 1e-6);
+        float* qi = qinfo + (int64_t)j * QI_LEN;
+        qi[QI_QNORM] = __double2float_ru(qn);
+        qi[QI_SIGMA] = __double2float_ru(sigma);
+        qi[QI_CNORM] = __double2float_ru(cn);
+        qi[QI_PAD] = 0.0f;
+        tau[j] = __float_as_uint(kInf);
     }
 }
 
 cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
                           uint32_t* tau, cudaStream_t st) {
-    int QT = 12288 / idx.D;
-    QT = QT < 1 ? 1 : (QT > kRotMaxQT ? kRotMaxQT : QT);
-    const size_t smem = (size_t)QT * idx.D * sizeof(double);
-    if (smem > 48 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(rotate_f64_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
-    dim3 grid((B + QT - 1) / QT, (idx.D_pad + kRotThreads - 1) / kRotThreads);
-    rotate_f64_kernel<<<grid, kRotThreads, smem, st>>>(xq, idx.pca_mean, idx.pca_rot, B, idx.D, idx.D_pad, QT, qrot,
-                                                      qinfo, tau);
+    query_norms_kernel<<<(B + 7) / 8, 256, 0, st>>>(xq, idx.pca_mean, B, idx.D, idx.D_pad, qinfo, tau);
+    dim3 grid((B + kRM - 1) / kRM, (idx.D_pad + kRN - 1) / kRN);
+    rotate_f64_kernel<<<grid, 256, 0, st>>>(xq, idx.pca_mean, idx.pca_rot, B, idx.D, idx.D_pad, qrot);
     return cudaGetLastError();
 }
 
@@ -273,7 +283,19 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
             const int c = scid[best_n + i];
             const float* cr = cent + (int64_t)c * D;
             double acc = 0.0;
-            for (int d = 0; d < D; ++d) {
+            int d = 0;
+            // 32 independent loads in flight per chunk; the fma chain stays sequential in d
+            for (; d + 32 <= D; d += 32) {
+                float cv[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) cv[i] = __ldg(cr + d + i);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const double df = (double)qv[d + i] - (double)cv[i];
+                    acc = fma(df, df, acc);
+                }
+            }
+            for (; d < D; ++d) {
                 const double df = (double)qv[d] - (double)__ldg(cr + d);
                 acc = fma(df, df, acc);
             }

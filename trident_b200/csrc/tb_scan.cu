@@ -42,6 +42,7 @@ struct ScanArgs {
     int32_t* cand_i;
     unsigned long long* stats;
     int D, D_pad, nb, K, nprobe, G;
+    int seed_rows;  // exact-prefix rows for queries without a finite threshold (0: off)
     float rho;
 };
 
@@ -107,35 +108,114 @@ __device__ __forceinline__ void load_block(const uint8_t* __restrict__ p, uint4&
     w1 = __ldg(reinterpret_cast<const uint4*>(p + 16));
 }
 
+// Float codes of one 32-dim block (exact uint8 -> float) for the register-resident first block.
+__device__ __forceinline__ void unpack_block(const uint4 w0, const uint4 w1, float* cf) {
+    const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) cf[4 * i + k] = u8f(w[i], k);
+}
+
+// Stage Y on one block whose codes are already floats.
+__device__ __forceinline__ float lb_block_f(const float* cf, const float* __restrict__ base,
+                                            const float* __restrict__ dl, const float* __restrict__ ep, float acc) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 b4 = *reinterpret_cast<const float4*>(base + 4 * i);
+        const float4 d4 = *reinterpret_cast<const float4*>(dl + 4 * i);
+        const float4 e4 = *reinterpret_cast<const float4*>(ep + 4 * i);
+        float l;
+        l = fmaxf(fabsf(fmaf(cf[4 * i + 0], d4.x, b4.x)) - e4.x, 0.0f); acc = fmaf(l, l, acc);
+        l = fmaxf(fabsf(fmaf(cf[4 * i + 1], d4.y, b4.y)) - e4.y, 0.0f); acc = fmaf(l, l, acc);
+        l = fmaxf(fabsf(fmaf(cf[4 * i + 2], d4.z, b4.z)) - e4.z, 0.0f); acc = fmaf(l, l, acc);
+        l = fmaxf(fabsf(fmaf(cf[4 * i + 3], d4.w, b4.w)) - e4.w, 0.0f); acc = fmaf(l, l, acc);
+    }
+    return acc;
+}
+
+// Stage Y / UB on one block beyond the shared-memory window: base = vmin - q~ is formed in
+// registers from global (L1-resident) vmin and q~, with the same float32 subtraction as the
+// shared-memory copy, so the bound is identical on both paths.
+template <bool UPPER>
+__device__ __forceinline__ float bound_block_g(const uint4 w0, const uint4 w1, const float* __restrict__ vm,
+                                               const float* __restrict__ qr, const float* __restrict__ dl,
+                                               const float* __restrict__ ep, float acc) {
+    const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v4 = __ldg(reinterpret_cast<const float4*>(vm) + i);
+        const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr) + i);
+        const float4 d4 = *reinterpret_cast<const float4*>(dl + 4 * i);
+        const float4 e4 = *reinterpret_cast<const float4*>(ep + 4 * i);
+        const float b[4] = {v4.x - q4.x, v4.y - q4.y, v4.z - q4.z, v4.w - q4.w};
+        const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
+        const float ee[4] = {e4.x, e4.y, e4.z, e4.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float u = fabsf(fmaf(u8f(w[i], k), dd[k], b[k]));
+            const float l = UPPER ? u + ee[k] : fmaxf(u - ee[k], 0.0f);
+            acc = fmaf(l, l, acc);
+        }
+    }
+    return acc;
+}
+
+constexpr int kNBS = 4;  // leading 32-dim blocks whose per-query base is staged in shared memory
+constexpr int kGC = 4;   // queries per Stage-Y chunk: a chunk adds at most kGC * T queue entries
+constexpr int kQM = 12;  // deep-queue and survivor-list capacity, in units of T entries
+
+// Survivor / deep-queue entry: query slot j (5 bits) and list-local row r (27 bits).
+__device__ __forceinline__ uint32_t pack_jr(int j, int r) { return ((uint32_t)j << 27) | (uint32_t)r; }
+__device__ __forceinline__ int entry_j(uint32_t e) { return (int)(e >> 27); }
+__device__ __forceinline__ int entry_r(uint32_t e) { return (int)(e & 0x7FFFFFFu); }
+
 template <int T, int KM, bool LB, bool UB, bool VEC4>
 __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
     constexpr int NW = T / 32;
+    constexpr int QCAP = kQM * T;
     extern __shared__ __align__(16) unsigned char smem[];
     const int G = a.G;
     const int D_pad = a.D_pad;
+    const int nb = a.nb;
+    const int nbs = nb < kNBS ? nb : kNBS;  // staged blocks
+    const int BW = nbs * 32;                // staged width per query
     float* s_base = reinterpret_cast<float*>(smem);
-    float* s_dl = s_base + (LB ? G * D_pad : 0);
+    float* s_dl = s_base + (LB ? G * BW : 0);
     float* s_ep = s_dl + (LB ? D_pad : 0);
     float* s_topd = s_ep + (LB ? D_pad : 0);
     int32_t* s_topi = reinterpret_cast<int32_t*>(s_topd + G * KM);
-    float* s_sd = reinterpret_cast<float*>(s_topi + G * KM);
-    uint16_t* s_sq = reinterpret_cast<uint16_t*>(s_sd + G * T);
+    uint32_t* s_sv = reinterpret_cast<uint32_t*>(s_topi + G * KM);  // [QCAP] survivors (j, r)
+    float* s_sd = reinterpret_cast<float*>(s_sv + QCAP);            // [QCAP] their exact distances
+    uint32_t* s_qe = reinterpret_cast<uint32_t*>(s_sd + QCAP);      // [2][QCAP] deep queue (j, r) (LB)
+    float* s_qa = reinterpret_cast<float*>(s_qe + (LB ? 2 * QCAP : 0));  // [2][QCAP] partial bounds (LB)
 
-    __shared__ int32_t s_qid[kMaxG], s_pp[kMaxG], s_cnt[kMaxG], s_pref[kMaxG + 1];
+    __shared__ int32_t s_qid[kMaxG], s_pp[kMaxG], s_seed[kMaxG];
     __shared__ float s_tau[kMaxG], s_ts[kMaxG], s_sig[kMaxG];
-    __shared__ int s_item;
+    __shared__ int s_item, s_sn, s_qn[2], s_flag[2];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int K = a.K, D = a.D, nb = a.nb;
+    const int K = a.K, D = a.D;
     unsigned long long st_cand = 0, st_dims = 0, st_surv = 0, st_ins = 0, st_items = 0;
 
     for (;;) {
-        if (tid == 0) s_item = atomicAdd(a.work_ctr, 1);
+        if (tid == 0) {
+            s_item = atomicAdd(a.work_ctr, 1);
+            s_sn = 0;
+            s_qn[0] = 0;
+            s_qn[1] = 0;
+        }
         __syncthreads();
         const int it = s_item;
         if (it >= *a.n_items) break;
         const int4 item = a.items[it];
         const int c = item.x, pstart = item.y, n = item.z;
+        const int64_t r0 = a.row_off[c];
+        const int L = (int)(a.row_off[c + 1] - r0);
+        const int64_t t0 = a.tile_off[c];
+        const int nt = (L + T - 1) / T;
+        const float* vm_c = a.vmin + (int64_t)c * D_pad;
+        const uint8_t* codes_c = a.codes + (size_t)t0 * nb * T * 32;
         ++st_items;
         if (tid < n) {
             const int q = a.pair_q[pstart + tid];
@@ -146,19 +226,14 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             s_sig[tid] = sig;
             s_tau[tid] = tq;
             s_ts[tid] = prune_threshold(tq, sig, a.rho);
-            s_cnt[tid] = 0;
+            s_seed[tid] = 0;
         }
         if (LB) {
-            for (int d = tid; d < D_pad; d += T) {
-                s_dl[d] = __ldg(a.delta + (int64_t)c * D_pad + d);
-                s_ep[d] = __ldg(a.eps + (int64_t)c * D_pad + d);
-            }
-        }
-        __syncthreads();
-        if (LB) {
-            for (int i = tid; i < n * D_pad; i += T) {
-                const int j = i / D_pad, d = i - j * D_pad;
-                s_base[i] = __ldg(a.vmin + (int64_t)c * D_pad + d) - __ldg(a.qrot + (int64_t)s_qid[j] * D_pad + d);
+            const float4* d4 = reinterpret_cast<const float4*>(a.delta + (int64_t)c * D_pad);
+            const float4* e4 = reinterpret_cast<const float4*>(a.eps + (int64_t)c * D_pad);
+            for (int i = tid; i < D_pad / 4; i += T) {
+                reinterpret_cast<float4*>(s_dl)[i] = __ldg(d4 + i);
+                reinterpret_cast<float4*>(s_ep)[i] = __ldg(e4 + i);
             }
         }
         for (int i = tid; i < n * KM; i += T) {
@@ -166,42 +241,191 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             s_topi[i] = -1;
         }
         __syncthreads();
+        if (LB) {
+            // base_j = vmin_c - q~_j on the staged blocks, one warp per query, float4 over dims
+            const float4* vm4 = reinterpret_cast<const float4*>(vm_c);
+            for (int j = warp; j < n; j += NW) {
+                const float4* q4 = reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad);
+                float4* b4 = reinterpret_cast<float4*>(s_base + j * BW);
+                for (int i = lane; i < BW / 4; i += 32) {
+                    const float4 x = __ldg(vm4 + i), y = __ldg(q4 + i);
+                    b4[i] = make_float4(x.x - y.x, x.y - y.y, x.z - y.z, x.w - y.w);
+                }
+            }
+        }
+        __syncthreads();
 
-        const int64_t r0 = a.row_off[c];
-        const int L = (int)(a.row_off[c + 1] - r0);
-        const int64_t t0 = a.tile_off[c];
-        const int nt = (L + T - 1) / T;
+        // ---- Stage Z + per-query top-K insertion over the survivor list, then threshold exchange
+        auto refine = [&]() {
+            const int sn = s_sn;
+            for (int s = warp; s < sn; s += NW) {
+                const uint32_t e = s_sv[s];
+                const float* xr = a.xb + (r0 + entry_r(e)) * D;
+                const float* qr = a.xq + (int64_t)s_qid[entry_j(e)] * D;
+                const float dist = exact_dist_warp<VEC4>(xr, qr, D, lane);
+                if (lane == 0) s_sd[s] = dist;
+            }
+            __syncthreads();
+            for (int j = warp; j < n; j += NW) {
+                float* ld = s_topd + j * KM;
+                int32_t* li = s_topi + j * KM;
+                for (int k0 = 0; k0 < sn; k0 += 32) {
+                    const int k = k0 + lane;
+                    bool ok = false;
+                    float d = kInf;
+                    int32_t id = 0;
+                    if (k < sn) {
+                        const uint32_t e = s_sv[k];
+                        if (entry_j(e) == j) {
+                            ok = true;
+                            d = s_sd[k];
+                            id = __ldg(a.oid + r0 + entry_r(e));
+                        }
+                    }
+                    if (__any_sync(TB_FULL, ok)) st_ins += (unsigned)list_offer<KM>(ld, li, K, ok, d, id, lane);
+                }
+                if (lane == 0) {
+                    const float kth = ld[K - 1];
+                    const int q = s_qid[j];
+                    float tq = s_tau[j];
+                    if (kth < tq) {
+                        tq = kth;
+                        atomicMin(a.tau + q, __float_as_uint(kth));
+                    }
+                    const float g = ld_volatile_f32(a.tau + q);
+                    if (g < tq) tq = g;
+                    s_tau[j] = tq;
+                    s_ts[j] = prune_threshold(tq, s_sig[j], a.rho);
+                }
+            }
+            st_surv += (tid == 0) ? (unsigned long long)sn : 0ull;
+            __syncthreads();
+            if (tid == 0) s_sn = 0;
+            __syncthreads();
+        };
+
+        // push one survivor (j, r) (rare: per-thread atomics)
+        auto push_survivor = [&](int j, int r) {
+            const int p = atomicAdd(&s_sn, 1);
+            s_sv[p] = pack_jr(j, r);
+        };
+
+        // ---- deep queue: entries alive after the register-resident blocks, at level `lvl`.
+        // Dense levels while the queue fills the CTA, then one warp per remaining entry with its
+        // lanes evaluating all remaining blocks at once (one load round trip instead of a chain).
+        auto flush_deep = [&](int lvl) {
+            if (s_sn > 0) refine();
+            int cnt = s_qn[0];
+            int src = 0;
+            int b = lvl;
+            while (cnt > 2 * NW && b < nb) {
+                const int dst = src ^ 1;
+                for (int i0 = warp * 32; i0 < cnt; i0 += T) {
+                    const int i = i0 + lane;
+                    bool alive = false;
+                    uint32_t e = 0;
+                    float acc = 0.0f;
+                    if (i < cnt) {
+                        e = s_qe[src * QCAP + i];
+                        acc = s_qa[src * QCAP + i];
+                        const int j = entry_j(e), r = entry_r(e);
+                        uint4 w0, w1;
+                        load_block(codes_c + (((size_t)(r / T) * nb + b) * T + (r % T)) * 32, w0, w1);
+                        acc = b < nbs ? lb_block(w0, w1, s_base + j * BW + 32 * b, s_dl + 32 * b, s_ep + 32 * b, acc)
+                                      : bound_block_g<false>(w0, w1, vm_c + 32 * b,
+                                                             a.qrot + (int64_t)s_qid[j] * D_pad + 32 * b,
+                                                             s_dl + 32 * b, s_ep + 32 * b, acc);
+                        alive = acc <= s_ts[j];
+                        st_dims += 32u;
+                    }
+                    if (b == nb - 1) {
+                        if (alive) push_survivor(entry_j(e), entry_r(e));
+                    } else {
+                        const unsigned m = __ballot_sync(TB_FULL, alive);
+                        if (m) {
+                            const int leader = __ffs(m) - 1;
+                            int pos = 0;
+                            if (lane == leader) pos = atomicAdd(&s_qn[dst], __popc(m));
+                            pos = __shfl_sync(TB_FULL, pos, leader);
+                            if (alive) {
+                                const int p = pos + __popc(m & ((1u << lane) - 1u));
+                                s_qe[dst * QCAP + p] = e;
+                                s_qa[dst * QCAP + p] = acc;
+                            }
+                        }
+                    }
+                }
+                __syncthreads();
+                cnt = s_qn[dst];
+                if (tid == 0) s_qn[src] = 0;
+                src = dst;
+                ++b;
+                __syncthreads();
+            }
+            if (b < nb) {
+                for (int i = warp; i < cnt; i += NW) {
+                    const uint32_t e = s_qe[src * QCAP + i];
+                    const int j = entry_j(e), r = entry_r(e);
+                    const float* qr = a.qrot + (int64_t)s_qid[j] * D_pad;
+                    const uint8_t* rowc = codes_c + (size_t)(r / T) * nb * T * 32 + (size_t)(r % T) * 32;
+                    float part = 0.0f;
+                    for (int bb = b + lane; bb < nb; bb += 32) {
+                        uint4 w0, w1;
+                        load_block(rowc + (size_t)bb * T * 32, w0, w1);
+                        part += bb < nbs ? lb_block(w0, w1, s_base + j * BW + 32 * bb, s_dl + 32 * bb, s_ep + 32 * bb, 0.0f)
+                                         : bound_block_g<false>(w0, w1, vm_c + 32 * bb, qr + 32 * bb, s_dl + 32 * bb,
+                                                                s_ep + 32 * bb, 0.0f);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(TB_FULL, part, o);
+                    if (lane == 0) {
+                        st_dims += 32ull * (unsigned)(nb - b);
+                        if (s_qa[src * QCAP + i] + part <= s_ts[j]) push_survivor(j, r);
+                    }
+                }
+            }
+            __syncthreads();
+            if (tid == 0) { s_qn[0] = 0; s_qn[1] = 0; }
+            __syncthreads();
+        };
 
         // ---- Stage X (optional): seed each query's threshold from SQ8 upper bounds of this list
         if (UB) {
             for (int t = 0; t < nt; ++t) {
                 const int v = t * T + tid;
                 const bool valid = v < L;
-                const uint8_t* tp = a.codes + (size_t)(t0 + t) * nb * T * 32;
-                for (int j = 0; j < n; ++j) {
-                    float ub = kInf;
-                    if (valid) {
-                        float acc = 0.0f;
-                        for (int b = 0; b < nb; ++b) {
-                            uint4 w0, w1;
-                            load_block(tp + ((size_t)b * T + tid) * 32, w0, w1);
-                            acc = ub_block(w0, w1, s_base + j * D_pad + 32 * b, s_dl + 32 * b, s_ep + 32 * b, acc);
+                const uint8_t* tp = codes_c + (size_t)t * nb * T * 32;
+                for (int jc = 0; jc < n; jc += kQM) {
+                    const int je = min(n, jc + kQM);
+                    for (int j = jc; j < je; ++j) {
+                        float ub = kInf;
+                        if (valid) {
+                            const float* qr = a.qrot + (int64_t)s_qid[j] * D_pad;
+                            float acc = 0.0f;
+                            for (int b = 0; b < nb; ++b) {
+                                uint4 w0, w1;
+                                load_block(tp + ((size_t)b * T + tid) * 32, w0, w1);
+                                acc = b < nbs ? ub_block(w0, w1, s_base + j * BW + 32 * b, s_dl + 32 * b,
+                                                         s_ep + 32 * b, acc)
+                                              : bound_block_g<true>(w0, w1, vm_c + 32 * b, qr + 32 * b,
+                                                                    s_dl + 32 * b, s_ep + 32 * b, acc);
+                            }
+                            ub = acc;
                         }
-                        ub = acc;
+                        s_sd[(j - jc) * T + tid] = ub;
                     }
-                    s_sd[j * T + tid] = ub;
-                }
-                __syncthreads();
-                for (int j = warp; j < n; j += NW) {
-                    float* ld = s_topd + j * KM;
-                    int32_t* li = s_topi + j * KM;
-                    for (int k0 = 0; k0 < T; k0 += 32) {
-                        const int k = k0 + lane;
-                        const float ub = s_sd[j * T + k];
-                        list_offer<KM>(ld, li, K, ub < kInf, ub, t * T + k, lane);
+                    __syncthreads();
+                    for (int j = jc + warp; j < je; j += NW) {
+                        float* ld = s_topd + j * KM;
+                        int32_t* li = s_topi + j * KM;
+                        for (int k0 = 0; k0 < T; k0 += 32) {
+                            const int k = k0 + lane;
+                            const float ub = s_sd[(j - jc) * T + k];
+                            list_offer<KM>(ld, li, K, ub < kInf, ub, t * T + k, lane);
+                        }
                     }
+                    __syncthreads();
                 }
-                __syncthreads();
             }
             for (int j = warp; j < n; j += NW) {
                 float* ld = s_topd + j * KM;
@@ -222,115 +446,128 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             __syncthreads();
         }
 
+        // ---- Stage X (exact prefix): a query that reaches this list without a finite threshold
+        // (warm-up pass, or no warm-up at all) first gets the exact distances of the list's first
+        // S rows, so the rest of the list is pruned against their K-th distance. Tile 0's Stage Y
+        // then skips those rows for that query.
+        if (LB && a.seed_rows > 0) {
+            const int S = min(L, a.seed_rows);
+            if (tid < n && !(s_tau[tid] < kInf)) s_seed[tid] = S;
+            __syncthreads();
+            int ns = 0;
+            for (int j = 0; j < n; ++j) ns += s_seed[j] ? 1 : 0;
+            if (ns > 0) {
+                if (tid < n && s_seed[tid]) {
+                    st_cand += S;
+                    st_dims += (unsigned long long)S * D_pad;
+                }
+                const int qc = QCAP / S;  // queries whose seed rows fit the survivor list at once
+                for (int jc = 0; jc < n; jc += qc) {
+                    const int je = min(n, jc + qc);
+                    for (int i = tid; i < (je - jc) * S; i += T) {
+                        const int j = jc + i / S, r = i % S;
+                        if (s_seed[j]) {
+                            const int p = atomicAdd(&s_sn, 1);
+                            s_sv[p] = pack_jr(j, r);
+                        }
+                    }
+                    __syncthreads();
+                    refine();
+                }
+            }
+        }
+
         for (int t = 0; t < nt; ++t) {
             const int v = t * T + tid;
             const bool valid = v < L;
             const int Lt = min(T, L - t * T);
-            int total;
             if (LB) {
-                // ---- Stage Y: blocked SQ8 lower bound with warp early exit
-                const uint8_t* tp = a.codes + (size_t)(t0 + t) * nb * T * 32;
-                uint4 c0 = make_uint4(0, 0, 0, 0), c1 = make_uint4(0, 0, 0, 0);
-                if (valid) load_block(tp + (size_t)tid * 32, c0, c1);
-                for (int j = 0; j < n; ++j) {
-                    const float ts = s_ts[j];
-                    const float* bj = s_base + j * D_pad;
-                    float acc = lb_block(c0, c1, bj, s_dl, s_ep, 0.0f);
-                    bool alive = valid && acc <= ts;
-                    int used = 1;
-                    for (int b = 1; b < nb; ++b) {
-                        if (!__any_sync(TB_FULL, alive)) break;
-                        if (alive) {
-                            uint4 w0, w1;
-                            load_block(tp + ((size_t)b * T + tid) * 32, w0, w1);
-                            acc = lb_block(w0, w1, bj + 32 * b, s_dl + 32 * b, s_ep + 32 * b, acc);
-                            alive = acc <= ts;
-                            used = b + 1;
+                // ---- Stage Y: each thread holds its row's blocks 0 (as floats) and 1 (packed) in
+                // registers and evaluates them for every query of the item; rows still alive
+                // after block 1 go to the deep queue.
+                const uint8_t* tp = codes_c + (size_t)t * nb * T * 32;
+                float cf[32];
+                uint4 p0 = make_uint4(0, 0, 0, 0), p1 = make_uint4(0, 0, 0, 0);
+                {
+                    uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
+                    if (valid) {
+                        load_block(tp + (size_t)tid * 32, w0, w1);
+                        if (nb > 1) load_block(tp + ((size_t)T + tid) * 32, p0, p1);
+                    }
+                    unpack_block(w0, w1, cf);
+                }
+                for (int jc = 0; jc < n; jc += kGC) {
+                    // Room for this chunk: at most kGC * T new entries in each list. The counters
+                    // are sampled by one thread and broadcast through a barrier, so that every
+                    // thread takes the same branch (the flush and refine contain barriers) even
+                    // though fast warps start pushing as soon as they pass it.
+                    if (tid == 0) s_flag[0] = (s_qn[0] > QCAP - kGC * T ? 1 : 0) | (s_sn > QCAP - kGC * T ? 2 : 0);
+                    __syncthreads();
+                    const int f = s_flag[0];
+                    if (f & 1) flush_deep(2);
+                    if (f) {
+                        if (tid == 0) s_flag[1] = s_sn > QCAP - kGC * T;
+                        __syncthreads();
+                        if (s_flag[1]) refine();
+                    }
+                    const int je = min(n, jc + kGC);
+                    for (int j = jc; j < je; ++j) {
+                        const float ts = s_ts[j];
+                        const bool ok = valid && !(t == 0 && v < s_seed[j]);
+                        float acc = lb_block_f(cf, s_base + j * BW, s_dl, s_ep, 0.0f);
+                        bool alive = ok && acc <= ts;
+                        int used = 1;
+                        if (nb > 1 && __any_sync(TB_FULL, alive)) {
+                            if (alive) {
+                                acc = lb_block(p0, p1, s_base + j * BW + 32, s_dl + 32, s_ep + 32, acc);
+                                alive = acc <= ts;
+                                used = 2;
+                            }
+                        }
+                        if (ok) {
+                            st_cand += 1;
+                            st_dims += 32u * (unsigned)used;
+                        }
+                        // compaction (ballot / ffs leader / popc rank, reference :796-825)
+                        const unsigned m = __ballot_sync(TB_FULL, alive);
+                        if (m) {
+                            const int leader = __ffs(m) - 1;
+                            const int rank = __popc(m & ((1u << lane) - 1u));
+                            int pos = 0;
+                            if (nb <= 2) {
+                                if (lane == leader) pos = atomicAdd(&s_sn, __popc(m));
+                                pos = __shfl_sync(TB_FULL, pos, leader);
+                                if (alive) s_sv[pos + rank] = pack_jr(j, v);
+                            } else {
+                                if (lane == leader) pos = atomicAdd(&s_qn[0], __popc(m));
+                                pos = __shfl_sync(TB_FULL, pos, leader);
+                                if (alive) {
+                                    s_qe[pos + rank] = pack_jr(j, v);
+                                    s_qa[pos + rank] = acc;
+                                }
+                            }
                         }
                     }
-                    if (valid) {
-                        st_cand += 1;
-                        st_dims += 32u * (unsigned)used;
-                        st_surv += alive ? 1u : 0u;
-                    }
-                    // survivor compaction (ballot / ffs leader / popc rank, reference :796-825)
-                    const unsigned m = __ballot_sync(TB_FULL, alive);
-                    if (m) {
-                        const int leader = __ffs(m) - 1;
-                        int pos = 0;
-                        if (lane == leader) pos = atomicAdd(&s_cnt[j], __popc(m));
-                        pos = __shfl_sync(TB_FULL, pos, leader);
-                        if (alive) s_sq[j * T + pos + __popc(m & ((1u << lane) - 1u))] = (uint16_t)tid;
-                    }
+                    __syncthreads();
                 }
-                __syncthreads();
-                if (warp == 0) {
-                    int cj = lane < n ? s_cnt[lane] : 0;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const int x = __shfl_up_sync(TB_FULL, cj, o);
-                        if (lane >= o) cj += x;
-                    }
-                    s_pref[lane + 1] = cj;
-                    if (lane == 0) s_pref[0] = 0;
-                }
-                __syncthreads();
-                total = s_pref[n];
             } else {
-                if (valid) st_cand += n, st_surv += n;
-                total = n * Lt;
-            }
-
-            // ---- Stage Z: one warp per surviving (query, row), exact FP32 in the reference order
-            for (int s = warp; s < total; s += NW) {
-                int j, k, vv;
-                if (LB) {
-                    j = 0;
-                    while (j + 1 < n && s_pref[j + 1] <= s) ++j;
-                    k = s - s_pref[j];
-                    vv = s_sq[j * T + k];
-                } else {
-                    j = s / Lt;
-                    k = s - j * Lt;
-                    vv = k;
-                }
-                const float* xr = a.xb + (r0 + (int64_t)t * T + vv) * D;
-                const float* qr = a.xq + (int64_t)s_qid[j] * D;
-                const float dist = exact_dist_warp<VEC4>(xr, qr, D, lane);
-                if (lane == 0) s_sd[j * T + k] = dist;
-            }
-            __syncthreads();
-
-            // ---- per-query top-K insertion, then threshold exchange
-            for (int j = warp; j < n; j += NW) {
-                const int cj = LB ? s_cnt[j] : Lt;
-                float* ld = s_topd + j * KM;
-                int32_t* li = s_topi + j * KM;
-                for (int k0 = 0; k0 < cj; k0 += 32) {
-                    const int k = k0 + lane;
-                    const bool ok = k < cj;
-                    const float d = ok ? s_sd[j * T + k] : kInf;
-                    const int vv = ok ? (LB ? (int)s_sq[j * T + k] : k) : 0;
-                    const int32_t id = ok ? __ldg(a.oid + r0 + (int64_t)t * T + vv) : 0;
-                    st_ins += (unsigned)list_offer<KM>(ld, li, K, ok, d, id, lane);
-                }
-                if (lane == 0) {
-                    const float kth = ld[K - 1];
-                    const int q = s_qid[j];
-                    float tq = s_tau[j];
-                    if (kth < tq) {
-                        tq = kth;
-                        atomicMin(a.tau + q, __float_as_uint(kth));
+                // ---- CM-FP32: every row of the tile is refined for every query of the item
+                if (valid) st_cand += n;
+                for (int jc = 0; jc < n; jc += kGC) {
+                    if (s_sn > QCAP - kGC * T) refine();
+                    const int je = min(n, jc + kGC);
+                    for (int i = tid; i < (je - jc) * Lt; i += T) {
+                        const int j = jc + i / Lt, r = t * T + i % Lt;
+                        s_sv[s_sn + i] = pack_jr(j, r);
                     }
-                    const float g = ld_volatile_f32(a.tau + q);
-                    if (g < tq) tq = g;
-                    s_tau[j] = tq;
-                    s_ts[j] = prune_threshold(tq, s_sig[j], a.rho);
-                    s_cnt[j] = 0;
+                    __syncthreads();
+                    if (tid == 0) s_sn += (je - jc) * Lt;
+                    __syncthreads();
                 }
             }
-            __syncthreads();
         }
+        if (LB && s_qn[0] > 0) flush_deep(2);
+        if (s_sn > 0) refine();
 
         // ---- emit this item's per-query lists into the (query, probe) candidate slots
         for (int i = tid; i < n * K; i += T) {
@@ -435,11 +672,13 @@ static int km_for(int K) { return K <= 32 ? 32 : 128; }
 static size_t scan_smem(const trident_index& idx, int K, int G, bool lb) {
     const int T = idx.tile_size;
     const int KM = km_for(K);
+    const int nbs = idx.num_blocks < kNBS ? idx.num_blocks : kNBS;
+    const size_t qcap = (size_t)kQM * T;
     size_t s = 0;
-    if (lb) s += (size_t)(G + 2) * idx.D_pad * sizeof(float);
-    s += (size_t)G * KM * (sizeof(float) + sizeof(int32_t));
-    s += (size_t)G * T * sizeof(float);
-    s += (size_t)G * T * sizeof(uint16_t);
+    if (lb) s += ((size_t)G * nbs * 32 + 2 * (size_t)idx.D_pad) * sizeof(float);   // base, delta, eps
+    s += (size_t)G * KM * (sizeof(float) + sizeof(int32_t));                          // top-K lists
+    s += qcap * (sizeof(uint32_t) + sizeof(float));                                   // survivors + distances
+    if (lb) s += 2 * qcap * (sizeof(uint32_t) + sizeof(float));                        // deep queue (2 buffers)
     return s;
 }
 
@@ -511,6 +750,8 @@ cudaError_t launch_scan(const trident_index& idx, const float* xq, const Workspa
     a.K = sl.K;
     a.nprobe = sl.nprobe;
     a.G = sl.G;
+    a.seed_rows = sl.lb ? 32 * ((sl.K + 31) / 32) : 0;
+    if (a.seed_rows > idx.tile_size) a.seed_rows = idx.tile_size;
     a.rho = idx.lb_rel_slack;
     const bool vec4 = (idx.D % 4) == 0 && (((uintptr_t)idx.xb_sorted | (uintptr_t)xq) & 15) == 0;
     const size_t smem = scan_smem(idx, sl.K, sl.G, sl.lb != 0);
