@@ -156,6 +156,21 @@ int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t
                    void* workspace, size_t workspace_bytes, int32_t* probe_cids, double* probe_d64,
                    float* qrot, int64_t* stats, void* stream);
 
+/* Size of the fixed workspace behind trident_search_noalloc, per GPU. */
+#define TRIDENT_NOALLOC_WORKSPACE_BYTES (32u * 1024u * 1024u)
+
+/* trident_search for callers that cannot allocate device memory (no counterpart in the
+ * reference, whose caller always allocated the scratch tensors). Same arguments and results as
+ * trident_search without the workspace: the workspace is a TRIDENT_NOALLOC_WORKSPACE_BYTES array
+ * compiled into the library, held by every GPU that loads it until the process exits. Returns
+ * TRIDENT_ERR_WORKSPACE when trident_workspace_size(B, K, nprobe) exceeds that size. No call
+ * allocates. All calls on a device share the array: calls whose GPU work overlaps in time race
+ * and must be serialised by the caller. The first call on each device looks up the array's
+ * device address; make it before capturing a stream. */
+int trident_search_noalloc(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
+                           int32_t mode, int32_t ub_seed, float* out_d, int64_t* out_i, int64_t* stats,
+                           void* stream);
+
 /* Multi-GPU merge: R per-shard result lists d_in/i_in [R, B, K] (as gathered by an NCCL
  * all-gather) -> the global top-K per query under the (distance, id) order. */
 int trident_merge_shards(const float* d_in, const int64_t* i_in, int32_t R, int32_t B, int32_t K,

@@ -45,6 +45,8 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 namespace tb {
 
+int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 int num_sms() {
     static int cached[64] = {0};
     int dev = 0;

@@ -67,4 +67,7 @@ cudaError_t launch_merge_shards(const float* d_in, const int64_t* i_in, int R, i
 
 int num_sms();
 
+// Store `msg` as the calling thread's last error (trident_last_error) and return `code`.
+int record_error(int code, const char* msg);
+
 }  // namespace tb
