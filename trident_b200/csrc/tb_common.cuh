@@ -105,6 +105,19 @@ __device__ __forceinline__ void list_insert(float* ld, int32_t* li, int K, float
     __syncwarp();
 }
 
+// True when (d, id) is already among the first K entries (a row refined twice for one query
+// produces the bit-identical distance, so it must not take a second slot).
+template <int KM>
+__device__ __forceinline__ bool list_contains(const float* ld, const int32_t* li, int K, float d, int32_t id, int lane) {
+    bool hit = false;
+#pragma unroll
+    for (int m = 0; m < KM / 32; ++m) {
+        const int i = lane + 32 * m;
+        hit |= (i < K) && li[i] == id && ld[i] == d;
+    }
+    return __any_sync(TB_FULL, hit);
+}
+
 // Offer one candidate per lane (valid lanes only) to the list; returns the number inserted.
 template <int KM>
 __device__ __forceinline__ int list_offer(float* ld, int32_t* li, int K, bool valid, float d, int32_t id, int lane) {
@@ -119,7 +132,7 @@ __device__ __forceinline__ int list_offer(float* ld, int32_t* li, int K, bool va
         const int32_t si = __shfl_sync(TB_FULL, id, s);
         kd = ld[K - 1];
         ki = li[K - 1];
-        if (better(sd, si, kd, ki)) {
+        if (better(sd, si, kd, ki) && !list_contains<KM>(ld, li, K, sd, si, lane)) {
             list_insert<KM>(ld, li, K, sd, si, lane);
             ++inserted;
         }

@@ -42,7 +42,7 @@ struct ScanArgs {
     int32_t* cand_i;
     unsigned long long* stats;
     int D, D_pad, nb, K, nprobe, G;
-    int seed_rows;  // exact-prefix rows for queries without a finite threshold (0: off)
+    int seed_rows;  // best-ranked rows refined first for queries without a finite threshold (0: off)
     float rho;
 };
 
@@ -446,34 +446,61 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             __syncthreads();
         }
 
-        // ---- Stage X (exact prefix): a query that reaches this list without a finite threshold
-        // (warm-up pass, or no warm-up at all) first gets the exact distances of the list's first
-        // S rows, so the rest of the list is pruned against their K-th distance. Tile 0's Stage Y
-        // then skips those rows for that query.
+        // ---- Stage X (ranked seed): a query that reaches this list without a finite threshold
+        // (warm-up pass, or no warm-up at all) first ranks every row of the list by its block-0
+        // lower bound, refines the S best rows exactly, and starts from their K-th distance. The
+        // normal Stage Y then scans every row; a seed row refined again is not inserted twice.
         if (LB && a.seed_rows > 0) {
             const int S = min(L, a.seed_rows);
             if (tid < n && !(s_tau[tid] < kInf)) s_seed[tid] = S;
             __syncthreads();
             int ns = 0;
             for (int j = 0; j < n; ++j) ns += s_seed[j] ? 1 : 0;
-            if (ns > 0) {
-                if (tid < n && s_seed[tid]) {
-                    st_cand += S;
-                    st_dims += (unsigned long long)S * D_pad;
+            if (ns > 0 && S > 0) {
+                for (int t = 0; t < nt; ++t) {
+                    const int v = t * T + tid;
+                    float cf[32];
+                    {
+                        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
+                        if (v < L) load_block(codes_c + (size_t)t * nb * T * 32 + (size_t)tid * 32, w0, w1);
+                        unpack_block(w0, w1, cf);
+                    }
+                    for (int jc = 0; jc < n; jc += kQM) {
+                        const int je = min(n, jc + kQM);
+                        for (int j = jc; j < je; ++j)
+                            if (s_seed[j])
+                                s_sd[(j - jc) * T + tid] = v < L ? lb_block_f(cf, s_base + j * BW, s_dl, s_ep, 0.0f) : kInf;
+                        __syncthreads();
+                        for (int j = jc + warp; j < je; j += NW) {
+                            if (!s_seed[j]) continue;
+                            float* ld = s_topd + j * KM;
+                            int32_t* li = s_topi + j * KM;
+                            for (int k0 = 0; k0 < T; k0 += 32) {
+                                const int k = k0 + lane;
+                                const float lb = s_sd[(j - jc) * T + k];
+                                list_offer<KM>(ld, li, S, lb < kInf, lb, t * T + k, lane);
+                            }
+                        }
+                        __syncthreads();
+                    }
                 }
-                const int qc = QCAP / S;  // queries whose seed rows fit the survivor list at once
-                for (int jc = 0; jc < n; jc += qc) {
-                    const int je = min(n, jc + qc);
-                    for (int i = tid; i < (je - jc) * S; i += T) {
-                        const int j = jc + i / S, r = i % S;
-                        if (s_seed[j]) {
+                // the S best-ranked rows of each seeded query become survivors; the lists start over
+                for (int j = warp; j < n; j += NW) {
+                    if (!s_seed[j]) continue;
+                    float* ld = s_topd + j * KM;
+                    int32_t* li = s_topi + j * KM;
+                    for (int k = lane; k < S; k += 32) {
+                        const int32_t r = li[k];
+                        if (r >= 0) {
                             const int p = atomicAdd(&s_sn, 1);
                             s_sv[p] = pack_jr(j, r);
                         }
                     }
-                    __syncthreads();
-                    refine();
+                    __syncwarp();
+                    list_init<KM>(ld, li, lane);
                 }
+                __syncthreads();
+                refine();
             }
         }
 
@@ -513,7 +540,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     const int je = min(n, jc + kGC);
                     for (int j = jc; j < je; ++j) {
                         const float ts = s_ts[j];
-                        const bool ok = valid && !(t == 0 && v < s_seed[j]);
+                        const bool ok = valid;
                         float acc = lb_block_f(cf, s_base + j * BW, s_dl, s_ep, 0.0f);
                         bool alive = ok && acc <= ts;
                         int used = 1;
