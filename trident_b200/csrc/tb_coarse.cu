@@ -29,20 +29,20 @@ namespace tb {
 // k-slices staged in shared memory, 4 x 4 outputs per thread. The k order of every output stays
 // sequential, so the result is bit-identical to the oracle.
 // ------------------------------------------------------------------------------------------
-constexpr int kRM = 64, kRN = 64, kRK = 16;
+constexpr int kRM = 64, kRN = 128, kRK = 16;
 
 __global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict__ xq, const double* __restrict__ mu,
                                                         const double* __restrict__ R, int B, int D, int D_pad,
                                                         float* __restrict__ qrot) {
-    __shared__ double sQ[kRK][kRM + 1];
-    __shared__ double sR[kRK][kRN + 1];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    __shared__ __align__(16) double sQ[kRK][kRM];
+    __shared__ __align__(16) double sR[kRK][kRN];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // rows ty*4..+3, columns tx + 16*j
     const int m0 = blockIdx.x * kRM, n0 = blockIdx.y * kRN;
-    double acc[4][4];
+    double acc[4][8];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
     for (int k0 = 0; k0 < D; k0 += kRK) {
         const int kn = min(kRK, D - k0);
         for (int i = threadIdx.x; i < kRM * kRK; i += 256) {
@@ -57,13 +57,16 @@ __global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict
         }
         __syncthreads();
         for (int k = 0; k < kn; ++k) {
-            double a[4], b[4];
+            const double2 a01 = *reinterpret_cast<const double2*>(&sQ[k][ty * 4]);
+            const double2 a23 = *reinterpret_cast<const double2*>(&sQ[k][ty * 4 + 2]);
+            const double a[4] = {a01.x, a01.y, a23.x, a23.y};
+            double b[8];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) { a[i] = sQ[k][ty * 4 + i]; b[i] = sR[k][tx * 4 + i]; }
+            for (int j = 0; j < 8; ++j) b[j] = sR[k][tx + 16 * j];
 #pragma unroll
             for (int i = 0; i < 4; ++i)
 #pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+                for (int j = 0; j < 8; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
         }
         __syncthreads();
     }
@@ -72,8 +75,8 @@ __global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict
         const int gm = m0 + ty * 4 + i;
         if (gm >= B) continue;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int gn = n0 + tx * 4 + j;
+        for (int j = 0; j < 8; ++j) {
+            const int gn = n0 + tx + 16 * j;
             if (gn < D_pad) qrot[(int64_t)gm * D_pad + gn] = gn < D ? (float)acc[i][j] : 0.0f;
         }
     }
@@ -186,7 +189,9 @@ cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B,
 // Exact top-nprobe selection, one CTA per query.
 // ------------------------------------------------------------------------------------------
 constexpr int kSelThreads = 512;
-constexpr int kSelCap = 2048;  // sorted best (<= nprobe <= 1024) + one batch of re-check members
+constexpr int kSelNW = kSelThreads / 32;
+constexpr int kSelCap = 2048;        // sorted best (<= nprobe <= 1024) + one batch of re-check members
+constexpr int kSelSmemKeys = 8192;   // approximate distances cached in shared memory up to this nlist
 
 __device__ void bitonic_sort_kc(unsigned long long* key, int32_t* cid, int P) {
     for (int k = 2; k <= P; k <<= 1) {
@@ -209,59 +214,70 @@ __device__ void bitonic_sort_kc(unsigned long long* key, int32_t* cid, int P) {
     }
 }
 
+__device__ __forceinline__ int block_sum_sel(int v, int* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    v = __reduce_add_sync(TB_FULL, (unsigned)v);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    int s = 0;
+#pragma unroll
+    for (int w = 0; w < kSelNW; ++w) s += red[w];
+    __syncthreads();
+    return s;
+}
+
+// float64 ||q - c||^2 in the oracle's order (oracle_l2_f64): lane l sums its contiguous chunk of
+// C = ceil(D/32) dims with fma, then the 32 chunk sums are added in lane order. Every lane returns
+// the total.
+__device__ __forceinline__ double l2_f64_warp(const float* __restrict__ qv, const float* __restrict__ cr, int D,
+                                              int lane) {
+    const int C = (D + 31) / 32;
+    const int d0 = lane * C, d1 = min(D, d0 + C);
+    double acc = 0.0;
+    for (int d = d0; d < d1; ++d) {
+        const double df = (double)qv[d] - (double)__ldg(cr + d);
+        acc = fma(df, df, acc);
+    }
+    double total = __shfl_sync(TB_FULL, acc, 0);
+#pragma unroll
+    for (int l = 1; l < 32; ++l) total += __shfl_sync(TB_FULL, acc, l);
+    return total;
+}
+
 __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
     const float* __restrict__ coarse, const float* __restrict__ xq, const float* __restrict__ cent,
     const float* __restrict__ qinfo, int nlist, int D, int nprobe, float cmax, int32_t* __restrict__ probe,
     double* __restrict__ probe_d64, unsigned long long* __restrict__ stats) {
-    extern __shared__ float qv[];  // [D]
+    extern __shared__ float sel_smem[];
+    float* qv = sel_smem;                                              // [D]
+    uint32_t* skeys = reinterpret_cast<uint32_t*>(sel_smem + ((D + 3) & ~3));  // [nlist] when cached
     __shared__ unsigned long long skey[kSelCap];
     __shared__ int32_t scid[kSelCap];
-    __shared__ uint32_t hist[256];
-    __shared__ uint32_t s_bucket, s_k;
+    __shared__ int red[kSelNW];
     __shared__ int s_batch;
     const int j = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* row = coarse + (int64_t)j * nlist;
+    const bool cached = nlist <= kSelSmemKeys;
     for (int d = tid; d < D; d += blockDim.x) qv[d] = xq[(int64_t)j * D + d];
+    if (cached)
+        for (int c = tid; c < nlist; c += blockDim.x) skeys[c] = float_key(__ldg(row + c));
+    __syncthreads();
 
-    // 1) radix select of the nprobe-th smallest approximate value (4 x 8-bit digits)
-    uint32_t prefix = 0, pmask = 0;
-    uint32_t kk = (uint32_t)nprobe;
-    for (int shift = 24; shift >= 0; shift -= 8) {
-        for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
-        __syncthreads();
+    // 1) the nprobe-th smallest approximate value, bit by bit from the top: bit b of the answer is
+    //    0 iff at least nprobe keys are <= (answer so far with bit b = 0 and all lower bits = 1)
+    uint32_t ans = 0;
+    for (int b = 31; b >= 0; --b) {
+        const uint32_t upper = ans | ((1u << b) - 1u);
+        int cnt = 0;
         for (int c = tid; c < nlist; c += blockDim.x) {
-            const uint32_t key = float_key(__ldg(row + c));
-            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> shift) & 255u], 1u);
+            const uint32_t k = cached ? skeys[c] : float_key(__ldg(row + c));
+            cnt += k <= upper;
         }
-        __syncthreads();
-        if (warp == 0) {
-            uint32_t h[8], s = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) { h[i] = hist[lane * 8 + i]; s += h[i]; }
-            uint32_t incl = s;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t n = __shfl_up_sync(TB_FULL, incl, o);
-                if (lane >= o) incl += n;
-            }
-            const uint32_t excl = incl - s;
-            if (excl < kk && kk <= incl) {
-                uint32_t cum = excl;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    if (cum + h[i] >= kk) { s_bucket = lane * 8 + i; s_k = kk - cum; break; }
-                    cum += h[i];
-                }
-            }
-        }
-        __syncthreads();
-        prefix |= s_bucket << shift;
-        pmask |= 0xFFu << shift;
-        kk = s_k;
-        __syncthreads();
+        cnt = block_sum_sel(cnt, red);
+        if (cnt < nprobe) ans |= (1u << b);
     }
-    const float t = key_float(prefix);
+    const float t = key_float(ans);
 
     // 2) members: approximate value within the certified band above t
     const double u = 5.9604644775390625e-08;
@@ -278,28 +294,11 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
     __syncthreads();
     long long members = 0;
     auto process_batch = [&]() {
-        // exact float64 distance of each batch member, then sort best + batch by (d64, cid)
-        for (int i = tid; i < batch; i += blockDim.x) {
+        // exact float64 distance of each batch member (one warp per member), then sort best + batch
+        for (int i = warp; i < batch; i += kSelNW) {
             const int c = scid[best_n + i];
-            const float* cr = cent + (int64_t)c * D;
-            double acc = 0.0;
-            int d = 0;
-            // 32 independent loads in flight per chunk; the fma chain stays sequential in d
-            for (; d + 32 <= D; d += 32) {
-                float cv[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) cv[i] = __ldg(cr + d + i);
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const double df = (double)qv[d + i] - (double)cv[i];
-                    acc = fma(df, df, acc);
-                }
-            }
-            for (; d < D; ++d) {
-                const double df = (double)qv[d] - (double)__ldg(cr + d);
-                acc = fma(df, df, acc);
-            }
-            skey[best_n + i] = (unsigned long long)__double_as_longlong(acc);
+            const double d64 = l2_f64_warp(qv, cent + (int64_t)c * D, D, lane);
+            if (lane == 0) skey[best_n + i] = (unsigned long long)__double_as_longlong(d64);
         }
         const int n = best_n + batch;
         int P = 1;
@@ -314,7 +313,7 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
     };
     for (int cs = 0; cs < nlist; cs += blockDim.x) {
         const int c = cs + tid;
-        const bool mem = (c < nlist) && (__ldg(row + c) <= thr);
+        const bool mem = (c < nlist) && ((cached ? key_float(skeys[c]) : __ldg(row + c)) <= thr);
         const int chunk = __syncthreads_count(mem);
         if (chunk == 0) continue;
         members += chunk;
@@ -345,12 +344,10 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
 cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B, int nprobe, const float* coarse,
                                 const float* qinfo, int32_t* probe, double* probe_d64, unsigned long long* stats,
                                 cudaStream_t st) {
-    const size_t smem = (size_t)idx.D * sizeof(float);
-    if (smem > 16 * 1024) {
-        cudaError_t e =
-            cudaFuncSetAttribute(probe_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-    }
+    size_t smem = (size_t)((idx.D + 3) & ~3) * sizeof(float);
+    if (idx.nlist <= kSelSmemKeys) smem += (size_t)idx.nlist * sizeof(uint32_t);
+    cudaError_t e = cudaFuncSetAttribute(probe_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
     probe_select_kernel<<<B, kSelThreads, smem, st>>>(coarse, xq, idx.centroids, qinfo, idx.nlist, idx.D, nprobe,
                                                       idx.centroid_norm_max, probe, probe_d64, stats);
     return cudaGetLastError();

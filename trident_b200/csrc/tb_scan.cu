@@ -161,6 +161,22 @@ __device__ __forceinline__ float bound_block_g(const uint4 w0, const uint4 w1, c
     return acc;
 }
 
+constexpr float kU32 = 5.9604644775390625e-08f;  // 2^-24
+constexpr int kSCS = 196;  // floats per query of scaled block-0/1 intervals: 16 groups x 12, +4 (banks)
+constexpr int kWB = 64;    // per-warp block-1 batch capacity
+
+// One 4-dim group of the scaled bound: two packed FFMA2 for u' = c * delta' + base', four
+// saturating |u'| - eps', two packed FFMA2 into the running pair of partial sums.
+__device__ __forceinline__ float2 scaled_group(const float2 c01, const float2 c23, const float4 dd, const float4 bb,
+                                               const float4 ee, float2 acc) {
+    const float2 u01 = __ffma2_rn(c01, make_float2(dd.x, dd.y), make_float2(bb.x, bb.y));
+    const float2 u23 = __ffma2_rn(c23, make_float2(dd.z, dd.w), make_float2(bb.z, bb.w));
+    const float l0 = __saturatef(fabsf(u01.x) - ee.x), l1 = __saturatef(fabsf(u01.y) - ee.y);
+    const float l2 = __saturatef(fabsf(u23.x) - ee.z), l3 = __saturatef(fabsf(u23.y) - ee.w);
+    acc = __ffma2_rn(make_float2(l0, l1), make_float2(l0, l1), acc);
+    return __ffma2_rn(make_float2(l2, l3), make_float2(l2, l3), acc);
+}
+
 constexpr int kNBS = 4;  // leading 32-dim blocks whose per-query base is staged in shared memory
 constexpr int kGC = 4;   // queries per Stage-Y chunk: a chunk adds at most kGC * T queue entries
 constexpr int kQM = 12;  // deep-queue and survivor-list capacity, in units of T entries
@@ -189,9 +205,13 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
     float* s_sd = reinterpret_cast<float*>(s_sv + QCAP);            // [QCAP] their exact distances
     uint32_t* s_qe = reinterpret_cast<uint32_t*>(s_sd + QCAP);      // [2][QCAP] deep queue (j, r) (LB)
     float* s_qa = reinterpret_cast<float*>(s_qe + (LB ? 2 * QCAP : 0));  // [2][QCAP] partial bounds (LB)
+    float* s_sc = s_qa + (LB ? 2 * QCAP : 0);                           // [G][kSCS] scaled intervals (LB)
+    float* s_wba = s_sc + (LB ? G * kSCS : 0);                          // [NW][kWB] block-1 batch bounds
+    uint8_t* s_wbl = reinterpret_cast<uint8_t*>(s_wba + (LB ? NW * kWB : 0));  // [NW][kWB] batch lanes
+    uint8_t* s_wbj = s_wbl + (LB ? NW * kWB : 0);                       // [NW][kWB] batch queries
 
     __shared__ int32_t s_qid[kMaxG], s_pp[kMaxG], s_seed[kMaxG];
-    __shared__ float s_tau[kMaxG], s_ts[kMaxG], s_sig[kMaxG];
+    __shared__ float s_tau[kMaxG], s_ts[kMaxG], s_sig[kMaxG], s_scale[kMaxG], s_s2inv[kMaxG], s_tsp[kMaxG];
     __shared__ int s_item, s_sn, s_qn[2], s_flag[2];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -227,6 +247,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             s_tau[tid] = tq;
             s_ts[tid] = prune_threshold(tq, sig, a.rho);
             s_seed[tid] = 0;
+            s_scale[tid] = 1.0f;
         }
         if (LB) {
             const float4* d4 = reinterpret_cast<const float4*>(a.delta + (int64_t)c * D_pad);
@@ -295,7 +316,10 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     const float g = ld_volatile_f32(a.tau + q);
                     if (g < tq) tq = g;
                     s_tau[j] = tq;
-                    s_ts[j] = prune_threshold(tq, s_sig[j], a.rho);
+                    const float ts = prune_threshold(tq, s_sig[j], a.rho);
+                    s_ts[j] = ts;
+                    const float sc = s_scale[j];
+                    s_tsp[j] = (ts < kInf) ? ts * sc * sc * (1.0f + 64.0f * kU32) : kInf;
                 }
             }
             st_surv += (tid == 0) ? (unsigned long long)sn : 0ull;
@@ -504,14 +528,44 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             }
         }
 
+        // ---- per-query scaled intervals for blocks 0 and 1. With s_j = 1/sqrt(prune threshold),
+        // l'_d = sat(|fma(c, delta_d s_j, base_jd s_j)| - eps'_jd) <= s_j l_d (eps' adds the float32
+        // roundings of the scaled terms), and clamping at 1 only lowers the bound; the scaled
+        // threshold stays <= 1 as tau tightens. Two dims go through one packed FFMA2.
+        if (LB) {
+            const int nsc = min(nb, 2) * 8;  // 4-dim groups staged
+            if (tid < n) {
+                const float ts = s_ts[tid];
+                const float sc = (ts < kInf) ? 1.0f / sqrtf(fmaxf(ts, 1e-30f)) : 1.0f;
+                s_scale[tid] = sc;
+                s_s2inv[tid] = (ts < kInf) ? 1.0f / (sc * sc) * (1.0f - 4.0f * kU32) : 1.0f;
+                s_tsp[tid] = (ts < kInf) ? ts * sc * sc * (1.0f + 64.0f * kU32) : kInf;
+            }
+            __syncthreads();
+            for (int i = tid; i < n * nsc * 4; i += T) {
+                const int j = i / (nsc * 4), d = i - j * (nsc * 4);
+                const int g = d >> 2, k = d & 3;
+                const float sc = s_scale[j];
+                const float b = s_base[j * BW + d];
+                const float dl = s_dl[d];
+                float* P = s_sc + j * kSCS + g * 12;
+                P[k] = dl * sc;
+                P[4 + k] = b * sc;
+                P[8 + k] = (s_ep[d] * sc + 2.0001f * kU32 * sc * (255.0f * dl + fabsf(b))) * (1.0f + 3.0f * kU32);
+            }
+            __syncthreads();
+        }
+
         for (int t = 0; t < nt; ++t) {
             const int v = t * T + tid;
             const bool valid = v < L;
             const int Lt = min(T, L - t * T);
             if (LB) {
-                // ---- Stage Y: each thread holds its row's blocks 0 (as floats) and 1 (packed) in
-                // registers and evaluates them for every query of the item; rows still alive
-                // after block 1 go to the deep queue.
+                // ---- Stage Y: each thread holds its row's block-0 codes as floats and block-1 codes
+                // packed in registers. Block 0 runs for every query of the item with full warps; the
+                // rows alive after it are batched per warp and their block 1 is evaluated densely,
+                // codes fetched from the owning lane by shuffles. Rows alive after block 1 go to the
+                // item's deep queue.
                 const uint8_t* tp = codes_c + (size_t)t * nb * T * 32;
                 float cf[32];
                 uint4 p0 = make_uint4(0, 0, 0, 0), p1 = make_uint4(0, 0, 0, 0);
@@ -523,58 +577,121 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     }
                     unpack_block(w0, w1, cf);
                 }
+                uint8_t* wb_l = s_wbl + warp * kWB;
+                uint8_t* wb_j = s_wbj + warp * kWB;
+                float* wb_a = s_wba + warp * kWB;
+                int wcnt = 0;  // warp-uniform fill of this warp's block-1 batch
+                // evaluate block 1 for the first `cnt` batched entries, keep the rest
+                auto run_batch = [&](int cnt) {
+                    const bool has = lane < cnt;
+                    const int r = has ? wb_l[lane] : 0;
+                    const int jj = has ? wb_j[lane] : 0;
+                    float acc = has ? wb_a[lane] : 0.0f;
+                    uint32_t w[8];
+                    w[0] = __shfl_sync(TB_FULL, p0.x, r); w[1] = __shfl_sync(TB_FULL, p0.y, r);
+                    w[2] = __shfl_sync(TB_FULL, p0.z, r); w[3] = __shfl_sync(TB_FULL, p0.w, r);
+                    w[4] = __shfl_sync(TB_FULL, p1.x, r); w[5] = __shfl_sync(TB_FULL, p1.y, r);
+                    w[6] = __shfl_sync(TB_FULL, p1.z, r); w[7] = __shfl_sync(TB_FULL, p1.w, r);
+                    const float4* P = reinterpret_cast<const float4*>(s_sc + jj * kSCS) + 24;
+                    float2 a2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+                    for (int g = 0; g < 8; ++g) {
+                        const float4 dd = P[3 * g], bb = P[3 * g + 1], ee = P[3 * g + 2];
+                        a2 = scaled_group(make_float2(u8f(w[g], 0), u8f(w[g], 1)), make_float2(u8f(w[g], 2), u8f(w[g], 3)),
+                                          dd, bb, ee, a2);
+                    }
+                    acc += a2.x + a2.y;
+                    const bool alive = has && acc <= s_tsp[jj];
+                    if (has) st_dims += 32u;
+                    const unsigned m = __ballot_sync(TB_FULL, alive);
+                    if (m) {
+                        const int leader = __ffs(m) - 1;
+                        const int rank = __popc(m & ((1u << lane) - 1u));
+                        int pos = 0;
+                        const int row = t * T + warp * 32 + r;
+                        if (nb <= 2) {
+                            if (lane == leader) pos = atomicAdd(&s_sn, __popc(m));
+                            pos = __shfl_sync(TB_FULL, pos, leader);
+                            if (alive) s_sv[pos + rank] = pack_jr(jj, row);
+                        } else {
+                            if (lane == leader) pos = atomicAdd(&s_qn[0], __popc(m));
+                            pos = __shfl_sync(TB_FULL, pos, leader);
+                            if (alive) {
+                                s_qe[pos + rank] = pack_jr(jj, row);
+                                s_qa[pos + rank] = acc * s_s2inv[jj];  // back to unscaled units
+                            }
+                        }
+                    }
+                    // move the unprocessed tail [cnt, wcnt) to the front
+                    const int rest = wcnt - cnt;
+                    uint8_t tl = 0, tj = 0;
+                    float ta = 0.0f;
+                    if (lane < rest) { tl = wb_l[cnt + lane]; tj = wb_j[cnt + lane]; ta = wb_a[cnt + lane]; }
+                    __syncwarp();
+                    if (lane < rest) { wb_l[lane] = tl; wb_j[lane] = tj; wb_a[lane] = ta; }
+                    __syncwarp();
+                    wcnt = rest;
+                };
                 for (int jc = 0; jc < n; jc += kGC) {
-                    // Room for this chunk: at most kGC * T new entries in each list. The counters
-                    // are sampled by one thread and broadcast through a barrier, so that every
-                    // thread takes the same branch (the flush and refine contain barriers) even
-                    // though fast warps start pushing as soon as they pass it.
-                    if (tid == 0) s_flag[0] = (s_qn[0] > QCAP - kGC * T ? 1 : 0) | (s_sn > QCAP - kGC * T ? 2 : 0);
+                    // Room until the next check: at most (kGC + 2) * T new entries in each list (this
+                    // chunk's rows, plus up to 31 entries per warp carried in the warp batches, plus the
+                    // batch flushed at the end of the tile). The counters are sampled by one
+                    // thread and broadcast through a barrier, so that every thread takes the same branch
+                    // (the flush and refine contain barriers) even though fast warps start pushing as
+                    // soon as they pass it.
+                    if (tid == 0)
+                        s_flag[0] = (s_qn[0] > QCAP - (kGC + 2) * T ? 1 : 0) | (s_sn > QCAP - (kGC + 2) * T ? 2 : 0);
                     __syncthreads();
                     const int f = s_flag[0];
                     if (f & 1) flush_deep(2);
                     if (f) {
-                        if (tid == 0) s_flag[1] = s_sn > QCAP - kGC * T;
+                        if (tid == 0) s_flag[1] = s_sn > QCAP - (kGC + 2) * T;
                         __syncthreads();
                         if (s_flag[1]) refine();
                     }
                     const int je = min(n, jc + kGC);
                     for (int j = jc; j < je; ++j) {
-                        const float ts = s_ts[j];
-                        const bool ok = valid;
-                        float acc = lb_block_f(cf, s_base + j * BW, s_dl, s_ep, 0.0f);
-                        bool alive = ok && acc <= ts;
-                        int used = 1;
-                        if (nb > 1 && __any_sync(TB_FULL, alive)) {
-                            if (alive) {
-                                acc = lb_block(p0, p1, s_base + j * BW + 32, s_dl + 32, s_ep + 32, acc);
-                                alive = acc <= ts;
-                                used = 2;
-                            }
+                        const float4* P = reinterpret_cast<const float4*>(s_sc + j * kSCS);
+                        float2 a2 = make_float2(0.0f, 0.0f);
+#pragma unroll
+                        for (int g = 0; g < 8; ++g) {
+                            const float4 dd = P[3 * g], bb = P[3 * g + 1], ee = P[3 * g + 2];
+                            a2 = scaled_group(make_float2(cf[4 * g], cf[4 * g + 1]), make_float2(cf[4 * g + 2], cf[4 * g + 3]),
+                                              dd, bb, ee, a2);
                         }
-                        if (ok) {
+                        const float acc = a2.x + a2.y;
+                        const bool alive = valid && acc <= s_tsp[j];
+                        if (valid) {
                             st_cand += 1;
-                            st_dims += 32u * (unsigned)used;
+                            st_dims += 32u;
                         }
                         // compaction (ballot / ffs leader / popc rank, reference :796-825)
                         const unsigned m = __ballot_sync(TB_FULL, alive);
                         if (m) {
-                            const int leader = __ffs(m) - 1;
-                            const int rank = __popc(m & ((1u << lane) - 1u));
-                            int pos = 0;
-                            if (nb <= 2) {
+                            if (nb == 1) {
+                                const int leader = __ffs(m) - 1;
+                                int pos = 0;
                                 if (lane == leader) pos = atomicAdd(&s_sn, __popc(m));
                                 pos = __shfl_sync(TB_FULL, pos, leader);
-                                if (alive) s_sv[pos + rank] = pack_jr(j, v);
+                                if (alive) s_sv[pos + __popc(m & ((1u << lane) - 1u))] = pack_jr(j, v);
                             } else {
-                                if (lane == leader) pos = atomicAdd(&s_qn[0], __popc(m));
-                                pos = __shfl_sync(TB_FULL, pos, leader);
                                 if (alive) {
-                                    s_qe[pos + rank] = pack_jr(j, v);
-                                    s_qa[pos + rank] = acc;
+                                    const int p = wcnt + __popc(m & ((1u << lane) - 1u));
+                                    wb_l[p] = (uint8_t)lane;
+                                    wb_j[p] = (uint8_t)j;
+                                    wb_a[p] = acc;
                                 }
+                                __syncwarp();
+                                wcnt += __popc(m);
+                                if (wcnt >= 32) run_batch(32);
                             }
                         }
                     }
+                    __syncthreads();
+                }
+                if (nb > 1) {
+                    // the tile's block-1 codes leave the registers: finish this warp's batch
+                    if (wcnt > 0) run_batch(wcnt);
                     __syncthreads();
                 }
             } else {
@@ -706,6 +823,8 @@ static size_t scan_smem(const trident_index& idx, int K, int G, bool lb) {
     s += (size_t)G * KM * (sizeof(float) + sizeof(int32_t));                          // top-K lists
     s += qcap * (sizeof(uint32_t) + sizeof(float));                                   // survivors + distances
     if (lb) s += 2 * qcap * (sizeof(uint32_t) + sizeof(float));                        // deep queue (2 buffers)
+    if (lb) s += (size_t)G * kSCS * sizeof(float);                                    // scaled intervals
+    if (lb) s += (size_t)(T / 32) * kWB * (sizeof(float) + 2);                         // block-1 batches
     return s;
 }
 
