@@ -120,7 +120,10 @@ int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, doubl
  *   ub_seed  0: warm-up lists only; 1: also seed the warm-up lists' threshold from SQ8 upper
  *            bounds; 2: seed every pass (the reference's TRIDENT_UB_SEED, :1262, now an argument);
  *   out_d    [B, K] float32 squared distances ascending; out_i [B, K] int64 original ids;
- *            ties are broken by the smaller id; missing results are (+inf, -1);
+ *            ties are broken by the smaller id; missing results are (+inf, -1). Every row
+ *            reads (NaN, -2) if a bounded wait inside the scan gave up, since a candidate may
+ *            then be missing (not expected in normal operation; the call still returns 0
+ *            because the check runs on the device after the launch);
  *   stats    optional int64[TRIDENT_STATS_LEN] accumulated counters (NULL to skip). */
 int trident_search(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
                    int32_t mode, int32_t ub_seed, void* workspace, size_t workspace_bytes,

@@ -152,5 +152,6 @@ __device__ __forceinline__ float key_float(uint32_t k) {
 __device__ __forceinline__ float ld_volatile_f32(const uint32_t* p) {
     return __uint_as_float(*reinterpret_cast<const volatile uint32_t*>(p));
 }
+__device__ __forceinline__ int32_t ld_volatile_i32(const int32_t* p) { return *reinterpret_cast<const volatile int32_t*>(p); }
 
 }  // namespace tb

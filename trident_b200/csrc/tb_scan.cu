@@ -41,6 +41,7 @@ struct ScanArgs {
     float* cand_d;
     int32_t* cand_i;
     unsigned long long* stats;
+    int32_t* err;  // set to 1 if a per-query lock wait gave up (results then marked invalid)
     int D, D_pad, nb, K, nprobe, G;
     int seed_rows;  // best-ranked rows refined first for queries without a finite threshold (0: off)
     float rho;
@@ -164,6 +165,8 @@ __device__ __forceinline__ float bound_block_g(const uint4 w0, const uint4 w1, c
 constexpr float kU32 = 5.9604644775390625e-08f;  // 2^-24
 constexpr int kSCS = 196;  // floats per query of scaled block-0/1 intervals: 16 groups x 12, +4 (banks)
 constexpr int kWB = 64;    // per-warp block-1 batch capacity
+constexpr int kWQ = 64;    // per-warp deep-queue capacity (<= 31 waiting + 32 new entries)
+constexpr int kLockSpins = 1 << 22;  // bounded wait for a per-query insertion lock
 
 // One 4-dim group of the scaled bound: two packed FFMA2 for u' = c * delta' + base', four
 // saturating |u'| - eps', two packed FFMA2 into the running pair of partial sums.
@@ -177,9 +180,10 @@ __device__ __forceinline__ float2 scaled_group(const float2 c01, const float2 c2
     return __ffma2_rn(make_float2(l2, l3), make_float2(l2, l3), acc);
 }
 
-constexpr int kNBS = 4;  // leading 32-dim blocks whose per-query base is staged in shared memory
-constexpr int kGC = 4;   // queries per Stage-Y chunk: a chunk adds at most kGC * T queue entries
-constexpr int kQM = 12;  // deep-queue and survivor-list capacity, in units of T entries
+constexpr int kNBS = 8;  // leading 32-dim blocks whose per-query base is staged in shared memory
+constexpr int kGC = 4;   // queries per CM-FP32 chunk: a chunk adds at most kGC * T survivors
+constexpr int kQM = 4;   // survivor-list capacity in units of T entries (>= kGC, >= the seed count)
+constexpr int kNBR = 1;  // code blocks a lane loads per deep-queue round (2 and 4 measured slower)
 
 // Survivor / deep-queue entry: query slot j (5 bits) and list-local row r (27 bits).
 __device__ __forceinline__ uint32_t pack_jr(int j, int r) { return ((uint32_t)j << 27) | (uint32_t)r; }
@@ -196,23 +200,25 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
     const int nb = a.nb;
     const int nbs = nb < kNBS ? nb : kNBS;  // staged blocks
     const int BW = nbs * 32;                // staged width per query
+    const int BWS = BW + 4;                 // its stride: rows of different queries start in different banks
     float* s_base = reinterpret_cast<float*>(smem);
-    float* s_dl = s_base + (LB ? G * BW : 0);
+    float* s_dl = s_base + (LB ? G * BWS : 0);
     float* s_ep = s_dl + (LB ? D_pad : 0);
     float* s_topd = s_ep + (LB ? D_pad : 0);
     int32_t* s_topi = reinterpret_cast<int32_t*>(s_topd + G * KM);
     uint32_t* s_sv = reinterpret_cast<uint32_t*>(s_topi + G * KM);  // [QCAP] survivors (j, r)
     float* s_sd = reinterpret_cast<float*>(s_sv + QCAP);            // [QCAP] their exact distances
-    uint32_t* s_qe = reinterpret_cast<uint32_t*>(s_sd + QCAP);      // [2][QCAP] deep queue (j, r) (LB)
-    float* s_qa = reinterpret_cast<float*>(s_qe + (LB ? 2 * QCAP : 0));  // [2][QCAP] partial bounds (LB)
-    float* s_sc = s_qa + (LB ? 2 * QCAP : 0);                           // [G][kSCS] scaled intervals (LB)
+    float* s_sc = s_sd + QCAP;                                          // [G][kSCS] scaled intervals (LB)
     float* s_wba = s_sc + (LB ? G * kSCS : 0);                          // [NW][kWB] block-1 batch bounds
-    uint8_t* s_wbl = reinterpret_cast<uint8_t*>(s_wba + (LB ? NW * kWB : 0));  // [NW][kWB] batch lanes
+    float* s_wqa = s_wba + (LB ? NW * kWB : 0);                         // [NW][kWQ] deep-queue bounds
+    uint32_t* s_wqe = reinterpret_cast<uint32_t*>(s_wqa + (LB ? NW * kWQ : 0));  // [NW][kWQ] deep (j, r)
+    uint8_t* s_wbl = reinterpret_cast<uint8_t*>(s_wqe + (LB ? NW * kWQ : 0));    // [NW][kWB] batch lanes
     uint8_t* s_wbj = s_wbl + (LB ? NW * kWB : 0);                       // [NW][kWB] batch queries
+    uint8_t* s_wqb = s_wbj + (LB ? NW * kWB : 0);                       // [NW][kWQ] deep next block
 
     __shared__ int32_t s_qid[kMaxG], s_pp[kMaxG], s_seed[kMaxG];
     __shared__ float s_tau[kMaxG], s_ts[kMaxG], s_sig[kMaxG], s_scale[kMaxG], s_s2inv[kMaxG], s_tsp[kMaxG];
-    __shared__ int s_item, s_sn, s_qn[2], s_flag[2];
+    __shared__ int s_item, s_sn, s_lock[kMaxG];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = a.K, D = a.D;
@@ -222,8 +228,6 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
         if (tid == 0) {
             s_item = atomicAdd(a.work_ctr, 1);
             s_sn = 0;
-            s_qn[0] = 0;
-            s_qn[1] = 0;
         }
         __syncthreads();
         const int it = s_item;
@@ -248,6 +252,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             s_ts[tid] = prune_threshold(tq, sig, a.rho);
             s_seed[tid] = 0;
             s_scale[tid] = 1.0f;
+            s_lock[tid] = 0;
         }
         if (LB) {
             const float4* d4 = reinterpret_cast<const float4*>(a.delta + (int64_t)c * D_pad);
@@ -267,7 +272,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             const float4* vm4 = reinterpret_cast<const float4*>(vm_c);
             for (int j = warp; j < n; j += NW) {
                 const float4* q4 = reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad);
-                float4* b4 = reinterpret_cast<float4*>(s_base + j * BW);
+                float4* b4 = reinterpret_cast<float4*>(s_base + j * BWS);
                 for (int i = lane; i < BW / 4; i += 32) {
                     const float4 x = __ldg(vm4 + i), y = __ldg(q4 + i);
                     b4[i] = make_float4(x.x - y.x, x.y - y.y, x.z - y.z, x.w - y.w);
@@ -276,8 +281,9 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
         }
         __syncthreads();
 
-        // ---- Stage Z + per-query top-K insertion over the survivor list, then threshold exchange
-        auto refine = [&]() {
+        // ---- Stage Z + per-query top-K insertion over the survivor list, then the threshold exchange
+        // of query slots [jlo, jhi) (the slots whose lists hold exact distances only)
+        auto refine = [&](int jlo, int jhi) {
             const int sn = s_sn;
             for (int s = warp; s < sn; s += NW) {
                 const uint32_t e = s_sv[s];
@@ -287,7 +293,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                 if (lane == 0) s_sd[s] = dist;
             }
             __syncthreads();
-            for (int j = warp; j < n; j += NW) {
+            for (int j = jlo + warp; j < jhi; j += NW) {
                 float* ld = s_topd + j * KM;
                 int32_t* li = s_topi + j * KM;
                 for (int k0 = 0; k0 < sn; k0 += 32) {
@@ -334,85 +340,6 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             s_sv[p] = pack_jr(j, r);
         };
 
-        // ---- deep queue: entries alive after the register-resident blocks, at level `lvl`.
-        // Dense levels while the queue fills the CTA, then one warp per remaining entry with its
-        // lanes evaluating all remaining blocks at once (one load round trip instead of a chain).
-        auto flush_deep = [&](int lvl) {
-            if (s_sn > 0) refine();
-            int cnt = s_qn[0];
-            int src = 0;
-            int b = lvl;
-            while (cnt > 2 * NW && b < nb) {
-                const int dst = src ^ 1;
-                for (int i0 = warp * 32; i0 < cnt; i0 += T) {
-                    const int i = i0 + lane;
-                    bool alive = false;
-                    uint32_t e = 0;
-                    float acc = 0.0f;
-                    if (i < cnt) {
-                        e = s_qe[src * QCAP + i];
-                        acc = s_qa[src * QCAP + i];
-                        const int j = entry_j(e), r = entry_r(e);
-                        uint4 w0, w1;
-                        load_block(codes_c + (((size_t)(r / T) * nb + b) * T + (r % T)) * 32, w0, w1);
-                        acc = b < nbs ? lb_block(w0, w1, s_base + j * BW + 32 * b, s_dl + 32 * b, s_ep + 32 * b, acc)
-                                      : bound_block_g<false>(w0, w1, vm_c + 32 * b,
-                                                             a.qrot + (int64_t)s_qid[j] * D_pad + 32 * b,
-                                                             s_dl + 32 * b, s_ep + 32 * b, acc);
-                        alive = acc <= s_ts[j];
-                        st_dims += 32u;
-                    }
-                    if (b == nb - 1) {
-                        if (alive) push_survivor(entry_j(e), entry_r(e));
-                    } else {
-                        const unsigned m = __ballot_sync(TB_FULL, alive);
-                        if (m) {
-                            const int leader = __ffs(m) - 1;
-                            int pos = 0;
-                            if (lane == leader) pos = atomicAdd(&s_qn[dst], __popc(m));
-                            pos = __shfl_sync(TB_FULL, pos, leader);
-                            if (alive) {
-                                const int p = pos + __popc(m & ((1u << lane) - 1u));
-                                s_qe[dst * QCAP + p] = e;
-                                s_qa[dst * QCAP + p] = acc;
-                            }
-                        }
-                    }
-                }
-                __syncthreads();
-                cnt = s_qn[dst];
-                if (tid == 0) s_qn[src] = 0;
-                src = dst;
-                ++b;
-                __syncthreads();
-            }
-            if (b < nb) {
-                for (int i = warp; i < cnt; i += NW) {
-                    const uint32_t e = s_qe[src * QCAP + i];
-                    const int j = entry_j(e), r = entry_r(e);
-                    const float* qr = a.qrot + (int64_t)s_qid[j] * D_pad;
-                    const uint8_t* rowc = codes_c + (size_t)(r / T) * nb * T * 32 + (size_t)(r % T) * 32;
-                    float part = 0.0f;
-                    for (int bb = b + lane; bb < nb; bb += 32) {
-                        uint4 w0, w1;
-                        load_block(rowc + (size_t)bb * T * 32, w0, w1);
-                        part += bb < nbs ? lb_block(w0, w1, s_base + j * BW + 32 * bb, s_dl + 32 * bb, s_ep + 32 * bb, 0.0f)
-                                         : bound_block_g<false>(w0, w1, vm_c + 32 * bb, qr + 32 * bb, s_dl + 32 * bb,
-                                                                s_ep + 32 * bb, 0.0f);
-                    }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(TB_FULL, part, o);
-                    if (lane == 0) {
-                        st_dims += 32ull * (unsigned)(nb - b);
-                        if (s_qa[src * QCAP + i] + part <= s_ts[j]) push_survivor(j, r);
-                    }
-                }
-            }
-            __syncthreads();
-            if (tid == 0) { s_qn[0] = 0; s_qn[1] = 0; }
-            __syncthreads();
-        };
-
         // ---- Stage X (optional): seed each query's threshold from SQ8 upper bounds of this list
         if (UB) {
             for (int t = 0; t < nt; ++t) {
@@ -429,7 +356,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                             for (int b = 0; b < nb; ++b) {
                                 uint4 w0, w1;
                                 load_block(tp + ((size_t)b * T + tid) * 32, w0, w1);
-                                acc = b < nbs ? ub_block(w0, w1, s_base + j * BW + 32 * b, s_dl + 32 * b,
+                                acc = b < nbs ? ub_block(w0, w1, s_base + j * BWS + 32 * b, s_dl + 32 * b,
                                                          s_ep + 32 * b, acc)
                                               : bound_block_g<true>(w0, w1, vm_c + 32 * b, qr + 32 * b,
                                                                     s_dl + 32 * b, s_ep + 32 * b, acc);
@@ -493,7 +420,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                         const int je = min(n, jc + kQM);
                         for (int j = jc; j < je; ++j)
                             if (s_seed[j])
-                                s_sd[(j - jc) * T + tid] = v < L ? lb_block_f(cf, s_base + j * BW, s_dl, s_ep, 0.0f) : kInf;
+                                s_sd[(j - jc) * T + tid] = v < L ? lb_block_f(cf, s_base + j * BWS, s_dl, s_ep, 0.0f) : kInf;
                         __syncthreads();
                         for (int j = jc + warp; j < je; j += NW) {
                             if (!s_seed[j]) continue;
@@ -508,23 +435,28 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                         __syncthreads();
                     }
                 }
-                // the S best-ranked rows of each seeded query become survivors; the lists start over
-                for (int j = warp; j < n; j += NW) {
-                    if (!s_seed[j]) continue;
-                    float* ld = s_topd + j * KM;
-                    int32_t* li = s_topi + j * KM;
-                    for (int k = lane; k < S; k += 32) {
-                        const int32_t r = li[k];
-                        if (r >= 0) {
-                            const int p = atomicAdd(&s_sn, 1);
-                            s_sv[p] = pack_jr(j, r);
+                // the S best-ranked rows of each seeded query become survivors, refined in groups of
+                // queries that fit the survivor list (S <= T <= QCAP); the lists start over
+                const int per = QCAP / S;
+                for (int jc = 0; jc < n; jc += per) {
+                    const int je = min(n, jc + per);
+                    for (int j = jc + warp; j < je; j += NW) {
+                        if (!s_seed[j]) continue;
+                        float* ld = s_topd + j * KM;
+                        int32_t* li = s_topi + j * KM;
+                        for (int k = lane; k < S; k += 32) {
+                            const int32_t r = li[k];
+                            if (r >= 0) {
+                                const int p = atomicAdd(&s_sn, 1);
+                                s_sv[p] = pack_jr(j, r);
+                            }
                         }
+                        __syncwarp();
+                        list_init<KM>(ld, li, lane);
                     }
-                    __syncwarp();
-                    list_init<KM>(ld, li, lane);
+                    __syncthreads();
+                    refine(jc, je);  // later slots still hold their ranking
                 }
-                __syncthreads();
-                refine();
             }
         }
 
@@ -546,7 +478,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                 const int j = i / (nsc * 4), d = i - j * (nsc * 4);
                 const int g = d >> 2, k = d & 3;
                 const float sc = s_scale[j];
-                const float b = s_base[j * BW + d];
+                const float b = s_base[j * BWS + d];
                 const float dl = s_dl[d];
                 float* P = s_sc + j * kSCS + g * 12;
                 P[k] = dl * sc;
@@ -556,16 +488,143 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
             __syncthreads();
         }
 
-        for (int t = 0; t < nt; ++t) {
-            const int v = t * T + tid;
-            const bool valid = v < L;
-            const int Lt = min(T, L - t * T);
-            if (LB) {
-                // ---- Stage Y: each thread holds its row's block-0 codes as floats and block-1 codes
-                // packed in registers. Block 0 runs for every query of the item with full warps; the
-                // rows alive after it are batched per warp and their block 1 is evaluated densely,
-                // codes fetched from the owning lane by shuffles. Rows alive after block 1 go to the
-                // item's deep queue.
+        if (LB) {
+            // ---- Stage Y/Z, warp-independent within the item. Each warp owns 32 rows of every tile:
+            //  * block 0 for every query of the item, full warps, codes as floats in registers;
+            //  * rows alive after block 0 are batched per warp; their block 1 runs densely with the
+            //    codes shuffled from the owning lane;
+            //  * rows alive after block 1 go to the warp's deep queue, advanced one block per lane per
+            //    round (entries at mixed levels), so a round's load latency overlaps other warps' work;
+            //  * a row that survives every block is refined at once by its warp (exact FP32, reference
+            //    order) and inserted into its query's top-K under a per-query lock; the query's
+            //    threshold tightens immediately for every warp.
+            // The CTA synchronises only when the item ends.
+            uint8_t* wb_l = s_wbl + warp * kWB;
+            uint8_t* wb_j = s_wbj + warp * kWB;
+            float* wb_a = s_wba + warp * kWB;
+            uint32_t* wq_e = s_wqe + warp * kWQ;
+            float* wq_a = s_wqa + warp * kWQ;
+            uint8_t* wq_b = s_wqb + warp * kWQ;
+            int wq_n = 0;  // warp-uniform deep-queue fill
+
+            // exact distance of list row r for query slot j (whole warp), insertion under the lock
+            auto refine_one = [&](int j, int r) {
+                const int q = s_qid[j];
+                const float gq = lane == 0 ? ld_volatile_f32(a.tau + q) : kInf;  // other CTAs' threshold
+                float dist = exact_dist_warp<VEC4>(a.xb + (r0 + r) * D, a.xq + (int64_t)q * D, D, lane);
+                dist = __shfl_sync(TB_FULL, dist, 0);
+                const int32_t id = __ldg(a.oid + r0 + r);
+                int got = 0;
+                if (lane == 0) {
+                    for (int spin = 0; spin < kLockSpins; ++spin) {
+                        if (atomicCAS(&s_lock[j], 0, 1) == 0) { got = 1; break; }
+                        __nanosleep(64);
+                    }
+                }
+                got = __shfl_sync(TB_FULL, got, 0);
+                if (!got) {  // never expected: the holder is a warp of this CTA doing one insertion
+                    if (lane == 0) atomicExch(a.err, 1);
+                    return;
+                }
+                __threadfence_block();
+                float* ld = s_topd + j * KM;
+                int32_t* li = s_topi + j * KM;
+                st_ins += (unsigned)list_offer<KM>(ld, li, K, lane == 0, dist, id, lane);
+                if (lane == 0) {
+                    st_surv += 1;
+                    const float kth = ld[K - 1];
+                    const float t_old = s_tau[j];
+                    const float tq = fminf(fminf(t_old, kth), gq);
+                    if (tq < t_old) {
+                        s_tau[j] = tq;
+                        const float ts = prune_threshold(tq, s_sig[j], a.rho);
+                        s_ts[j] = ts;
+                        const float sc = s_scale[j];
+                        s_tsp[j] = (ts < kInf) ? ts * sc * sc * (1.0f + 64.0f * kU32) : kInf;
+                    }
+                    __threadfence_block();
+                    atomicExch(&s_lock[j], 0);
+                    if (kth < t_old && kth < gq) atomicMin(a.tau + q, __float_as_uint(kth));
+                }
+                __syncwarp();
+            };
+
+            // One round over the first min(wq_n, 32 / g) deep entries with g = 2^lg lanes per entry.
+            // Lane `sub` of an entry loads its kNBR blocks b + sub + k g together, then adds their
+            // bounds while its own partial stays within the threshold; the group sums the partials.
+            // Every term is non-negative, so a lane that stops early already proves the entry dead,
+            // and a live entry has accounted for every block it advanced over (up to g kNBR).
+            // Steady state runs g = 1 (32 entries, kNBR consecutive blocks each); the drain at the
+            // end of an item widens g as the queue empties.
+            auto deep_round = [&](int lg) {
+                const int g = 1 << lg;
+                const int m = min(wq_n, 32 >> lg);
+                const int i = lane >> lg, sub = lane & (g - 1);
+                const bool has = i < m;
+                uint32_t e = 0;
+                float acc = 0.0f;
+                int b = nb;
+                if (has) {
+                    e = wq_e[i];
+                    acc = wq_a[i];
+                    b = wq_b[i];
+                }
+                const int j = entry_j(e), r = entry_r(e);
+                const uint8_t* rowc = codes_c + (size_t)(r / T) * nb * T * 32 + (size_t)(r % T) * 32;
+                const float* qr = a.qrot + (int64_t)s_qid[j] * D_pad;
+                uint4 w[kNBR][2];
+#pragma unroll
+                for (int k = 0; k < kNBR; ++k) {
+                    const int bb = b + sub + k * g;
+                    if (bb < nb) load_block(rowc + (size_t)bb * T * 32, w[k][0], w[k][1]);
+                }
+                const float ts = s_ts[j];
+                float part = sub == 0 ? acc : 0.0f;
+#pragma unroll
+                for (int k = 0; k < kNBR; ++k) {
+                    const int bb = b + sub + k * g;
+                    if (bb < nb && part <= ts) {
+                        part = bb < nbs ? lb_block(w[k][0], w[k][1], s_base + j * BWS + 32 * bb, s_dl + 32 * bb, s_ep + 32 * bb, part)
+                                        : bound_block_g<false>(w[k][0], w[k][1], vm_c + 32 * bb, qr + 32 * bb,
+                                                               s_dl + 32 * bb, s_ep + 32 * bb, part);
+                        st_dims += 32u;
+                    }
+                }
+                for (int o = g >> 1; o > 0; o >>= 1) part += __shfl_xor_sync(TB_FULL, part, o);
+                const int bn = min(b + g * kNBR, nb);
+                const bool lead = has && sub == 0;
+                const bool alive = lead && part <= ts;
+                const bool done = alive && bn == nb;
+                const bool keep = alive && bn < nb;
+                const int rest = wq_n - m;
+                uint32_t te = 0;
+                float ta = 0.0f;
+                uint8_t tb = 0;
+                if (lane < rest) { te = wq_e[m + lane]; ta = wq_a[m + lane]; tb = wq_b[m + lane]; }
+                __syncwarp();
+                const unsigned km = __ballot_sync(TB_FULL, keep);
+                const int nk = __popc(km);
+                if (keep) {
+                    const int p = __popc(km & ((1u << lane) - 1u));
+                    wq_e[p] = e;
+                    wq_a[p] = part;
+                    wq_b[p] = (uint8_t)bn;
+                }
+                if (lane < rest) { wq_e[nk + lane] = te; wq_a[nk + lane] = ta; wq_b[nk + lane] = tb; }
+                __syncwarp();
+                wq_n = nk + rest;
+                unsigned dm = __ballot_sync(TB_FULL, done);
+                while (dm) {
+                    const int s = __ffs(dm) - 1;
+                    dm &= dm - 1;
+                    const uint32_t es = __shfl_sync(TB_FULL, e, s);
+                    refine_one(entry_j(es), entry_r(es));
+                }
+            };
+
+            for (int t = 0; t < nt; ++t) {
+                const int v = t * T + tid;
+                const bool valid = v < L;
                 const uint8_t* tp = codes_c + (size_t)t * nb * T * 32;
                 float cf[32];
                 uint4 p0 = make_uint4(0, 0, 0, 0), p1 = make_uint4(0, 0, 0, 0);
@@ -577,11 +636,8 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     }
                     unpack_block(w0, w1, cf);
                 }
-                uint8_t* wb_l = s_wbl + warp * kWB;
-                uint8_t* wb_j = s_wbj + warp * kWB;
-                float* wb_a = s_wba + warp * kWB;
                 int wcnt = 0;  // warp-uniform fill of this warp's block-1 batch
-                // evaluate block 1 for the first `cnt` batched entries, keep the rest
+                // block 1 for the first `cnt` batched entries (codes shuffled from the owning lane)
                 auto run_batch = [&](int cnt) {
                     const bool has = lane < cnt;
                     const int r = has ? wb_l[lane] : 0;
@@ -603,24 +659,24 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     acc += a2.x + a2.y;
                     const bool alive = has && acc <= s_tsp[jj];
                     if (has) st_dims += 32u;
+                    const int row = t * T + warp * 32 + r;
                     const unsigned m = __ballot_sync(TB_FULL, alive);
-                    if (m) {
-                        const int leader = __ffs(m) - 1;
-                        const int rank = __popc(m & ((1u << lane) - 1u));
-                        int pos = 0;
-                        const int row = t * T + warp * 32 + r;
-                        if (nb <= 2) {
-                            if (lane == leader) pos = atomicAdd(&s_sn, __popc(m));
-                            pos = __shfl_sync(TB_FULL, pos, leader);
-                            if (alive) s_sv[pos + rank] = pack_jr(jj, row);
-                        } else {
-                            if (lane == leader) pos = atomicAdd(&s_qn[0], __popc(m));
-                            pos = __shfl_sync(TB_FULL, pos, leader);
-                            if (alive) {
-                                s_qe[pos + rank] = pack_jr(jj, row);
-                                s_qa[pos + rank] = acc * s_s2inv[jj];  // back to unscaled units
-                            }
+                    if (nb <= 2) {
+                        unsigned dm = m;
+                        while (dm) {
+                            const int s = __ffs(dm) - 1;
+                            dm &= dm - 1;
+                            refine_one(__shfl_sync(TB_FULL, jj, s), __shfl_sync(TB_FULL, row, s));
                         }
+                    } else if (m) {
+                        if (alive) {
+                            const int p = wq_n + __popc(m & ((1u << lane) - 1u));
+                            wq_e[p] = pack_jr(jj, row);
+                            wq_a[p] = acc * s_s2inv[jj];  // back to unscaled units
+                            wq_b[p] = 2;
+                        }
+                        __syncwarp();
+                        wq_n += __popc(m);
                     }
                     // move the unprocessed tail [cnt, wcnt) to the front
                     const int rest = wcnt - cnt;
@@ -632,73 +688,65 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     __syncwarp();
                     wcnt = rest;
                 };
-                for (int jc = 0; jc < n; jc += kGC) {
-                    // Room until the next check: at most (kGC + 2) * T new entries in each list (this
-                    // chunk's rows, plus up to 31 entries per warp carried in the warp batches, plus the
-                    // batch flushed at the end of the tile). The counters are sampled by one
-                    // thread and broadcast through a barrier, so that every thread takes the same branch
-                    // (the flush and refine contain barriers) even though fast warps start pushing as
-                    // soon as they pass it.
-                    if (tid == 0)
-                        s_flag[0] = (s_qn[0] > QCAP - (kGC + 2) * T ? 1 : 0) | (s_sn > QCAP - (kGC + 2) * T ? 2 : 0);
-                    __syncthreads();
-                    const int f = s_flag[0];
-                    if (f & 1) flush_deep(2);
-                    if (f) {
-                        if (tid == 0) s_flag[1] = s_sn > QCAP - (kGC + 2) * T;
-                        __syncthreads();
-                        if (s_flag[1]) refine();
-                    }
-                    const int je = min(n, jc + kGC);
-                    for (int j = jc; j < je; ++j) {
-                        const float4* P = reinterpret_cast<const float4*>(s_sc + j * kSCS);
-                        float2 a2 = make_float2(0.0f, 0.0f);
+                for (int j = 0; j < n; ++j) {
+                    const float4* P = reinterpret_cast<const float4*>(s_sc + j * kSCS);
+                    float2 a2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-                        for (int g = 0; g < 8; ++g) {
-                            const float4 dd = P[3 * g], bb = P[3 * g + 1], ee = P[3 * g + 2];
-                            a2 = scaled_group(make_float2(cf[4 * g], cf[4 * g + 1]), make_float2(cf[4 * g + 2], cf[4 * g + 3]),
-                                              dd, bb, ee, a2);
-                        }
-                        const float acc = a2.x + a2.y;
-                        const bool alive = valid && acc <= s_tsp[j];
-                        if (valid) {
-                            st_cand += 1;
-                            st_dims += 32u;
-                        }
-                        // compaction (ballot / ffs leader / popc rank, reference :796-825)
-                        const unsigned m = __ballot_sync(TB_FULL, alive);
-                        if (m) {
-                            if (nb == 1) {
-                                const int leader = __ffs(m) - 1;
-                                int pos = 0;
-                                if (lane == leader) pos = atomicAdd(&s_sn, __popc(m));
-                                pos = __shfl_sync(TB_FULL, pos, leader);
-                                if (alive) s_sv[pos + __popc(m & ((1u << lane) - 1u))] = pack_jr(j, v);
-                            } else {
-                                if (alive) {
-                                    const int p = wcnt + __popc(m & ((1u << lane) - 1u));
-                                    wb_l[p] = (uint8_t)lane;
-                                    wb_j[p] = (uint8_t)j;
-                                    wb_a[p] = acc;
-                                }
-                                __syncwarp();
-                                wcnt += __popc(m);
-                                if (wcnt >= 32) run_batch(32);
-                            }
-                        }
+                    for (int g = 0; g < 8; ++g) {
+                        const float4 dd = P[3 * g], bb = P[3 * g + 1], ee = P[3 * g + 2];
+                        a2 = scaled_group(make_float2(cf[4 * g], cf[4 * g + 1]), make_float2(cf[4 * g + 2], cf[4 * g + 3]),
+                                          dd, bb, ee, a2);
                     }
-                    __syncthreads();
+                    const float acc = a2.x + a2.y;
+                    const bool alive = valid && acc <= s_tsp[j];
+                    if (valid) {
+                        st_cand += 1;
+                        st_dims += 32u;
+                    }
+                    const unsigned m = __ballot_sync(TB_FULL, alive);
+                    if (!m) continue;
+                    if (nb == 1) {
+                        unsigned dm = m;
+                        while (dm) {
+                            const int s = __ffs(dm) - 1;
+                            dm &= dm - 1;
+                            refine_one(j, t * T + warp * 32 + s);
+                        }
+                        continue;
+                    }
+                    if (alive) {
+                        const int p = wcnt + __popc(m & ((1u << lane) - 1u));
+                        wb_l[p] = (uint8_t)lane;
+                        wb_j[p] = (uint8_t)j;
+                        wb_a[p] = acc;
+                    }
+                    __syncwarp();
+                    wcnt += __popc(m);
+                    if (wcnt >= 32) {
+                        run_batch(32);
+                        while (wq_n >= 32) deep_round(0);
+                    }
                 }
-                if (nb > 1) {
-                    // the tile's block-1 codes leave the registers: finish this warp's batch
-                    if (wcnt > 0) run_batch(wcnt);
-                    __syncthreads();
-                }
-            } else {
+                // the tile's block-1 codes leave the registers: finish this warp's batch
+                if (wcnt > 0) run_batch(wcnt);
+                while (wq_n >= 32) deep_round(0);
+            }
+            // drain the deep queue, giving each remaining entry as many lanes as fit
+            while (wq_n > 0) {
+                int lg = 0;
+                while (lg < 5 && (wq_n << (lg + 1)) <= 32) ++lg;
+                deep_round(lg);
+            }
+            __syncthreads();
+        } else {
+            for (int t = 0; t < nt; ++t) {
+                const int v = t * T + tid;
+                const bool valid = v < L;
+                const int Lt = min(T, L - t * T);
                 // ---- CM-FP32: every row of the tile is refined for every query of the item
                 if (valid) st_cand += n;
                 for (int jc = 0; jc < n; jc += kGC) {
-                    if (s_sn > QCAP - kGC * T) refine();
+                    if (s_sn > QCAP - kGC * T) refine(0, n);
                     const int je = min(n, jc + kGC);
                     for (int i = tid; i < (je - jc) * Lt; i += T) {
                         const int j = jc + i / Lt, r = t * T + i % Lt;
@@ -709,9 +757,8 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     __syncthreads();
                 }
             }
+            if (s_sn > 0) refine(0, n);
         }
-        if (LB && s_qn[0] > 0) flush_deep(2);
-        if (s_sn > 0) refine();
 
         // ---- emit this item's per-query lists into the (query, probe) candidate slots
         for (int i = tid; i < n * K; i += T) {
@@ -745,7 +792,7 @@ template <int KM>
 __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ cand_d, const int32_t* __restrict__ cand_i,
                                                    int B, int K, int nprobe, int p_lo, int p_hi,
                                                    uint32_t* __restrict__ tau_out, float* __restrict__ out_d,
-                                                   int64_t* __restrict__ out_i) {
+                                                   int64_t* __restrict__ out_i, const int32_t* __restrict__ err) {
     __shared__ float ld_all[8][KM];
     __shared__ int32_t li_all[8][KM];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -766,9 +813,12 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ ca
     }
     __syncwarp();
     if (out_d) {
+        // A scan whose bounded lock wait gave up may have dropped a candidate: every result row is
+        // then marked (NaN, -2) instead of being returned possibly incomplete.
+        const bool bad = ld_volatile_i32(err) != 0;
         for (int k = lane; k < K; k += 32) {
-            out_d[(int64_t)q * K + k] = ld[k];
-            out_i[(int64_t)q * K + k] = (int64_t)li[k];
+            out_d[(int64_t)q * K + k] = bad ? __int_as_float(0x7fc00000) : ld[k];
+            out_i[(int64_t)q * K + k] = bad ? (int64_t)-2 : (int64_t)li[k];
         }
     }
     // Every value ever stored in tau is the K-th distance of K distinct rows, hence an upper bound
@@ -819,12 +869,12 @@ static size_t scan_smem(const trident_index& idx, int K, int G, bool lb) {
     const int nbs = idx.num_blocks < kNBS ? idx.num_blocks : kNBS;
     const size_t qcap = (size_t)kQM * T;
     size_t s = 0;
-    if (lb) s += ((size_t)G * nbs * 32 + 2 * (size_t)idx.D_pad) * sizeof(float);   // base, delta, eps
+    if (lb) s += ((size_t)G * (nbs * 32 + 4) + 2 * (size_t)idx.D_pad) * sizeof(float);  // base, delta, eps
     s += (size_t)G * KM * (sizeof(float) + sizeof(int32_t));                          // top-K lists
     s += qcap * (sizeof(uint32_t) + sizeof(float));                                   // survivors + distances
-    if (lb) s += 2 * qcap * (sizeof(uint32_t) + sizeof(float));                        // deep queue (2 buffers)
     if (lb) s += (size_t)G * kSCS * sizeof(float);                                    // scaled intervals
     if (lb) s += (size_t)(T / 32) * kWB * (sizeof(float) + 2);                         // block-1 batches
+    if (lb) s += (size_t)(T / 32) * kWQ * (sizeof(float) + sizeof(uint32_t) + 1);      // deep queues
     return s;
 }
 
@@ -890,6 +940,7 @@ cudaError_t launch_scan(const trident_index& idx, const float* xq, const Workspa
     a.cand_d = ws.cand_d;
     a.cand_i = ws.cand_i;
     a.stats = stats;
+    a.err = ws.ctr + 15;
     a.D = idx.D;
     a.D_pad = idx.D_pad;
     a.nb = idx.num_blocks;
@@ -912,9 +963,11 @@ cudaError_t launch_merge(const Workspace& ws, int B, int K, int nprobe, int p_lo
                          float* out_d, int64_t* out_i, cudaStream_t st) {
     const int grid = (B + 7) / 8;
     if (K <= 32)
-        merge_kernel<32><<<grid, 256, 0, st>>>(ws.cand_d, ws.cand_i, B, K, nprobe, p_lo, p_hi, tau_out, out_d, out_i);
+        merge_kernel<32><<<grid, 256, 0, st>>>(ws.cand_d, ws.cand_i, B, K, nprobe, p_lo, p_hi, tau_out, out_d, out_i,
+                                                ws.ctr + 15);
     else
-        merge_kernel<128><<<grid, 256, 0, st>>>(ws.cand_d, ws.cand_i, B, K, nprobe, p_lo, p_hi, tau_out, out_d, out_i);
+        merge_kernel<128><<<grid, 256, 0, st>>>(ws.cand_d, ws.cand_i, B, K, nprobe, p_lo, p_hi, tau_out, out_d, out_i,
+                                                 ws.ctr + 15);
     return cudaGetLastError();
 }
 
