@@ -296,8 +296,7 @@ def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks):
     cids = cids.cpu().numpy()
     from trident_b200 import _lib
 
-    p_init = int(_lib.lib().trident_p_init(2, cfg.B, cfg.K, cfg.nprobe))
-    p1 = np.ascontiguousarray(cids[:, p_init:])
+    p1 = np.ascontiguousarray(cids)
     h = {"vec_off": idx.storage.cluster_vec_off.cpu().numpy(), "tile_off": idx.cluster_tile_off.cpu().numpy()}
     tau = out_d[:, cfg.K - 1].astype(np.float32)
     t0 = time.perf_counter()
@@ -444,7 +443,7 @@ def run_ours(args, d: Dist):
         if os.path.exists(pp):
             peaks = json.load(open(pp))
         ms_per_step = total_ms / args.steps
-        scan_ms = phase_tot["scan1"] / args.steps
+        scan_ms = phase_tot["scan"] / args.steps
         roof = None
         if not args.no_roofline and d.world == 1 and mode == 2:
             roof = roofline(idx, cfg, xq_dev, got_d, scan_ms, peaks)

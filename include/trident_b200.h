@@ -106,19 +106,25 @@ int trident_index_check(const trident_index* idx);
 int trident_workspace_size(const trident_index* idx, int32_t B, int32_t K, int32_t nprobe,
                            size_t* bytes);
 
-/* The warm-up split m_warm (p_init) the reference uses for mode 2 (:1264-1276). */
+/* The warm-up split m_warm (p_init) the reference uses for mode 2 (:1264-1276). The search seeds its
+ * thresholds from max(p_init, min(8, nprobe / 8)) nearest lists of each query. */
 int32_t trident_p_init(int32_t mode, int32_t B, int32_t K, int32_t nprobe);
 
 /* The cost router (phase4a_suite.py:1013-1035, 1079): returns TRIDENT_MODE_CM_FP32 when
  * W = B * nprobe * (N / nlist) * D < w0, else TRIDENT_MODE_CASCADE. w0 <= 0 selects 9.0e8. */
 int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, double w0);
 
-/* The whole query path, replacing launch_trident_v4_search (:1172-1604):
+/* The whole query path, replacing launch_trident_v4_search (:1172-1604). The cascade runs as
+ * coarse stage -> Stage X seed (each query's threshold from the best rows of its nearest lists,
+ * ranked by a partial SQ8 distance) -> one Stage Y/Z scan over every probe -> merge, where the
+ * reference ran a warm-up scan over its p_init lists before the main scan.
  *   xq       [B, D] float32 queries on the device;
  *   K        1..100 (the reference supported K = 10 only, :575, :984);
  *   mode     TRIDENT_MODE_{AUTO, CASCADE, CM_FP32};
- *   ub_seed  0: warm-up lists only; 1: also seed the warm-up lists' threshold from SQ8 upper
- *            bounds; 2: seed every pass (the reference's TRIDENT_UB_SEED, :1262, now an argument);
+ *   ub_seed  0: the Stage X seed refines its rows exactly; 1: it bounds them with SQ8 upper bounds
+ *            instead, reading no FP32 row (for rows in host memory); 2: as 1, and every scan work
+ *            item also seeds from upper bounds (the reference's TRIDENT_UB_SEED, :1262, now an
+ *            argument);
  *   out_d    [B, K] float32 squared distances ascending; out_i [B, K] int64 original ids;
  *            ties are broken by the smaller id; missing results are (+inf, -1). Every row
  *            reads (NaN, -2) if a bounded wait inside the scan gave up, since a candidate may
@@ -131,13 +137,12 @@ int trident_search(const trident_index* idx, const float* xq, int32_t B, int32_t
 
 /* Phases timed by trident_search_profiled. */
 enum trident_phase {
-    TRIDENT_PHASE_COARSE = 0,   /* rotation + coarse GEMM + exact probe selection   */
-    TRIDENT_PHASE_PAIRS = 1,    /* cluster-major pair lists and work items          */
-    TRIDENT_PHASE_SCAN0 = 2,    /* warm-up scan over the p_init nearest lists        */
-    TRIDENT_PHASE_MERGE0 = 3,   /* warm-up merge -> per-query threshold              */
-    TRIDENT_PHASE_SCAN1 = 4,    /* main scan over the remaining lists                */
-    TRIDENT_PHASE_MERGE1 = 5,   /* final top-K merge                                 */
-    TRIDENT_PHASES = 6
+    TRIDENT_PHASE_COARSE = 0,   /* rotation + coarse GEMM + exact probe selection            */
+    TRIDENT_PHASE_PAIRS = 1,    /* cluster-major pair lists and work items                   */
+    TRIDENT_PHASE_SEED = 2,     /* Stage X: per-query thresholds from the nearest lists      */
+    TRIDENT_PHASE_SCAN = 3,     /* Stage Y/Z (or CM-FP32) over every probed list             */
+    TRIDENT_PHASE_MERGE = 4,    /* final top-K merge                                         */
+    TRIDENT_PHASES = 5
 };
 
 /* trident_search plus CUDA-event timing of each phase (milliseconds, 0 for a phase that did not

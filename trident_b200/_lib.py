@@ -28,7 +28,7 @@ EXPORTED = (
     "trident_merge_shards", "trident_search_noalloc",
 )
 NOALLOC_WORKSPACE_BYTES = 32 * 1024 * 1024
-PHASES = ("coarse", "pairs", "scan0", "merge0", "scan1", "merge1")
+PHASES = ("coarse", "pairs", "seed", "scan", "merge")
 
 
 class TridentError(RuntimeError):

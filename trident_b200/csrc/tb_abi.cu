@@ -228,35 +228,29 @@ static int search_impl(const trident_index* idx, const float* xq, int32_t B, int
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
     g_launches += 4;
 
-    const int p_init = trident_p_init(mode, B, K, nprobe);
+    // One pass over every probe. The reference scans its p_init warm-up lists first to obtain the
+    // thresholds; here the query-major seed kernel takes that role before the scan starts.
     const int G = scan_group_size(*idx, K);
     TB_TRY(mark(TRIDENT_PHASE_PAIRS), "event");
-    TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, p_init, G, K, ws, st), "pairs");
+    TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, 0, G, K, ws, st), "pairs");
     g_launches += 4;
-
+    if (lb) {
+        TB_TRY(mark(TRIDENT_PHASE_SEED), "event");
+        TB_TRY(launch_seed(*idx, xq, ws, B, K, nprobe, seed_lists_for(B, K, nprobe), ub_seed >= 1, st), "seed");
+        g_launches += 1;
+    }
     ScanLaunch sl;
     sl.K = K;
     sl.nprobe = nprobe;
     sl.G = G;
     sl.lb = lb ? 1 : 0;
-    if (p_init > 0) {
-        sl.pass = 0;
-        sl.ub_seed = (lb && ub_seed >= 1) ? 1 : 0;
-        sl.max_items = B * p_init;
-        sl.item_base = 0;
-        TB_TRY(mark(TRIDENT_PHASE_SCAN0), "event");
-        TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan pass 0");
-        TB_TRY(mark(TRIDENT_PHASE_MERGE0), "event");
-        TB_TRY(launch_merge(ws, B, K, nprobe, 0, p_init, ws.tau, nullptr, nullptr, st), "merge pass 0");
-        g_launches += 2;
-    }
     sl.pass = 1;
-    sl.ub_seed = (lb && (ub_seed == 2 || (ub_seed == 1 && p_init == 0))) ? 1 : 0;
-    sl.max_items = B * (nprobe - p_init);
-    sl.item_base = (int64_t)B * p_init;
-    TB_TRY(mark(TRIDENT_PHASE_SCAN1), "event");
+    sl.ub_seed = (lb && ub_seed == 2) ? 1 : 0;
+    sl.max_items = B * nprobe;
+    sl.item_base = 0;
+    TB_TRY(mark(TRIDENT_PHASE_SCAN), "event");
     TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan pass 1");
-    TB_TRY(mark(TRIDENT_PHASE_MERGE1), "event");
+    TB_TRY(mark(TRIDENT_PHASE_MERGE), "event");
     TB_TRY(launch_merge(ws, B, K, nprobe, 0, nprobe, nullptr, out_d, out_i, st), "merge");
     g_launches += 2;
     TB_TRY(mark(TRIDENT_PHASES), "event");

@@ -27,6 +27,13 @@ __device__ __forceinline__ float u8f(uint32_t w, int k) {
     return __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)k)) - 8388608.0f;
 }
 
+// Bytes k and k+1 of w as exact floats: two PRMTs and one packed FADD.
+__device__ __forceinline__ float2 u8f2(uint32_t w, int k) {
+    const float2 t = make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)k)),
+                                 __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7440u | (uint32_t)(k + 1))));
+    return __fadd2_rn(t, make_float2(-8388608.0f, -8388608.0f));
+}
+
 // (d, id) strict order used by every top-K in the path (reference :26-31).
 __device__ __forceinline__ bool better(float d, int32_t id, float kd, int32_t kid) {
     return d < kd || (d == kd && id < kid);
@@ -35,34 +42,60 @@ __device__ __forceinline__ bool better(float d, int32_t id, float kd, int32_t ki
 // Exact FP32 squared L2 distance of one row against one query by a whole warp, in the
 // reference's order: lane l accumulates d = 4l + 128k + j, then the butterfly. Bit-identical to
 // the reference's CM-FP32 scan (:321-336) and Stage-Z refine (:870-883).
-template <bool VEC4>
+// With VEC4 (D % 4 == 0), NL chunks of 128 dims are loaded together before their FMAs (the
+// missing chunks of a lane's last batch are predicated off), so a 960-dim row costs ceil(8 / NL)
+// memory round trips instead of 8; each lane's FMA order is unchanged.
+template <bool VEC4, int NL = 1>
 __device__ __forceinline__ float exact_dist_warp(const float* __restrict__ x, const float* __restrict__ q,
                                                  int D, int lane) {
     float part = 0.0f;
     int d = lane * 4;
-    if (VEC4) {
-        for (; d + 3 < D; d += 128) {
-            const float4 xv = __ldg(reinterpret_cast<const float4*>(x + d));
-            const float4 qv = __ldg(reinterpret_cast<const float4*>(q + d));
-            float df0 = xv.x - qv.x; part = fmaf(df0, df0, part);
-            float df1 = xv.y - qv.y; part = fmaf(df1, df1, part);
-            float df2 = xv.z - qv.z; part = fmaf(df2, df2, part);
-            float df3 = xv.w - qv.w; part = fmaf(df3, df3, part);
-        }
-    } else {
-        for (; d + 3 < D; d += 128) {
+    if constexpr (VEC4 && NL > 1) {
+        for (; d < D; d += 128 * NL) {
+            float4 xv[NL], qv[NL];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                float df = __ldg(x + d + j) - __ldg(q + d + j);
-                part = fmaf(df, df, part);
+            for (int k = 0; k < NL; ++k) {
+                if (d + 128 * k < D) {
+                    xv[k] = __ldg(reinterpret_cast<const float4*>(x + d + 128 * k));
+                    qv[k] = __ldg(reinterpret_cast<const float4*>(q + d + 128 * k));
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < NL; ++k) {
+                if (d + 128 * k < D) {
+                    float df0 = xv[k].x - qv[k].x; part = fmaf(df0, df0, part);
+                    float df1 = xv[k].y - qv[k].y; part = fmaf(df1, df1, part);
+                    float df2 = xv[k].z - qv[k].z; part = fmaf(df2, df2, part);
+                    float df3 = xv[k].w - qv[k].w; part = fmaf(df3, df3, part);
+                }
             }
         }
+        return warp_sum_ref(part);
+    } else {
+        if constexpr (VEC4) {
+            for (; d + 3 < D; d += 128) {
+                const float4 xv = __ldg(reinterpret_cast<const float4*>(x + d));
+                const float4 qv = __ldg(reinterpret_cast<const float4*>(q + d));
+                float df0 = xv.x - qv.x; part = fmaf(df0, df0, part);
+                float df1 = xv.y - qv.y; part = fmaf(df1, df1, part);
+                float df2 = xv.z - qv.z; part = fmaf(df2, df2, part);
+                float df3 = xv.w - qv.w; part = fmaf(df3, df3, part);
+            }
+        } else {
+            for (; d + 3 < D; d += 128) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float df = __ldg(x + d + j) - __ldg(q + d + j);
+                    part = fmaf(df, df, part);
+                }
+            }
+        }
+        for (int dr = d; dr < d + 4 && dr < D; ++dr) {
+            float df = __ldg(x + dr) - __ldg(q + dr);
+            part = fmaf(df, df, part);
+        }
+        return warp_sum_ref(part);
     }
-    for (int dr = d; dr < d + 4 && dr < D; ++dr) {
-        float df = __ldg(x + dr) - __ldg(q + dr);
-        part = fmaf(df, df, part);
-    }
-    return warp_sum_ref(part);
 }
 
 // Warp-cooperative sorted top-K list in shared memory: ld/li hold K entries ascending by
@@ -153,5 +186,22 @@ __device__ __forceinline__ float ld_volatile_f32(const uint32_t* p) {
     return __uint_as_float(*reinterpret_cast<const volatile uint32_t*>(p));
 }
 __device__ __forceinline__ int32_t ld_volatile_i32(const int32_t* p) { return *reinterpret_cast<const volatile int32_t*>(p); }
+
+// Prune threshold for a query whose current K-th exact distance is tau: a row is dropped when its
+// partial bound exceeds (sqrt(tau (1 + rho)) + sigma)^2. rho covers the float32 accumulation of
+// the bound and of the exact distance, sigma the query-side roundings (Minkowski); the final
+// factor covers the roundings of this expression.
+__device__ __forceinline__ float prune_threshold(float tau, float sigma, float rho) {
+    if (!(tau < kInf)) return kInf;
+    const float s = sqrtf(tau * (1.0f + rho)) + sigma;
+    return s * s * (1.0f + 1e-6f);
+}
+
+// Threshold implied by an SQ8 upper bound ub of one row: its exact FP32 distance is at most this.
+__device__ __forceinline__ float ub_threshold(float ub, float sigma, float rho) {
+    if (!(ub < kInf)) return kInf;
+    const float s = sqrtf(ub * (1.0f + 2.0f * rho)) + sigma;
+    return s * s * (1.0f + 2.0f * rho) * (1.0f + 1e-6f);
+}
 
 }  // namespace tb

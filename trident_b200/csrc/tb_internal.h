@@ -46,6 +46,13 @@ cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B
 cudaError_t launch_pairs(const trident_index& idx, const int32_t* probe, int B, int nprobe, int p_init, int G, int K,
                          const Workspace& ws, cudaStream_t st);
 
+// Query-major threshold seeding (tb_seed.cu): rank the rows of each query's p_seed nearest lists by
+// a partial SQ8 distance, refine the best exactly (or bound them from above with ub) and store the
+// K-th value in ws.tau.
+int seed_lists_for(int B, int K, int nprobe);
+cudaError_t launch_seed(const trident_index& idx, const float* xq, const Workspace& ws, int B, int K, int nprobe,
+                        int p_seed, int ub, cudaStream_t st);
+
 // Scans and merges (tb_scan.cu).
 struct ScanLaunch {
     int pass;        // 0: warm-up lists, 1: the rest

@@ -49,23 +49,6 @@ struct ScanArgs {
 
 constexpr int kMaxG = 32;
 
-// Prune threshold for a query whose current K-th exact distance is tau: a row is dropped when its
-// partial bound exceeds (sqrt(tau (1 + rho)) + sigma)^2. rho covers the float32 accumulation of
-// the bound and of the exact distance, sigma the query-side roundings (Minkowski); the final
-// factor covers the roundings of this expression.
-__device__ __forceinline__ float prune_threshold(float tau, float sigma, float rho) {
-    if (!(tau < kInf)) return kInf;
-    const float s = sqrtf(tau * (1.0f + rho)) + sigma;
-    return s * s * (1.0f + 1e-6f);
-}
-
-// Threshold implied by an SQ8 upper bound ub of one row: its exact FP32 distance is at most this.
-__device__ __forceinline__ float ub_threshold(float ub, float sigma, float rho) {
-    if (!(ub < kInf)) return kInf;
-    const float s = sqrtf(ub * (1.0f + 2.0f * rho)) + sigma;
-    return s * s * (1.0f + 2.0f * rho) * (1.0f + 1e-6f);
-}
-
 // Stage Y on one 32-dim block: acc += sum_d max(|code_d delta_d + (vmin_d - q~_d)| - eps_d, 0)^2
 // (reference :750-767). base/dl/ep point at the block's 32 entries in shared memory.
 __device__ __forceinline__ float lb_block(const uint4 w0, const uint4 w1, const float* __restrict__ base,
@@ -289,7 +272,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                 const uint32_t e = s_sv[s];
                 const float* xr = a.xb + (r0 + entry_r(e)) * D;
                 const float* qr = a.xq + (int64_t)s_qid[entry_j(e)] * D;
-                const float dist = exact_dist_warp<VEC4>(xr, qr, D, lane);
+                const float dist = exact_dist_warp<VEC4, LB ? 1 : 4>(xr, qr, D, lane);
                 if (lane == 0) s_sd[s] = dist;
             }
             __syncthreads();

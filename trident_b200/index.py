@@ -286,7 +286,7 @@ class TridentV4Index:
         mode: 2 = TRIDENT cascade (K2), 10 = CM-FP32 exact scan, -1 = cost router. The reference's
         ablation modes (0 CM-SQ8+RR, 1 K1, 11 Tribase), use_l1 and rerank_m are not implemented.
         ub_seed replaces the reference's TRIDENT_UB_SEED environment variable. phase_ms (a dict)
-        receives CUDA-event times of each phase (coarse, pairs, scan0, merge0, scan1, merge1); the
+        receives CUDA-event times of each phase (coarse, pairs, seed, scan, merge); the
         call then synchronises the stream.
         """
         torch = _torch()
