@@ -318,7 +318,7 @@ def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks):
     achieved = bytes_alg / (scan_ms * 1e-3) / 1e9
     peak = float(peaks.get("hbm_gbs", 6650.0))
     return {
-        "bound": "hbm", "kernel": "scan_kernel (pass 1: Stage Y/Z)", "achieved": round(achieved, 1),
+        "bound": "hbm", "kernel": "scan_kernel (Stage Y/Z over every probe)", "achieved": round(achieved, 1),
         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(),
         "algorithmic_bytes": int(bytes_alg), "launch_ms": round(scan_ms, 4),
         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback 6.65 TB/s",
@@ -459,8 +459,9 @@ def run_ours(args, d: Dist):
                 "workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} nprobe={nprobe} K={K} B={B}",
                 "mode": {2: "cascade", 10: "cm_fp32"}[mode] + (" (router)" if args.mode == -1 else ""),
                 "ub_seed": args.ub_seed, "tile_size": idx.tile_size,
-                "l2": "inputs larger than L2 (0.96 GB SQ8 codes + 3.84 GB FP32 rows) and a 512 MB L2 flush "
-                      "between timed steps (outside the step events)",
+                "l2": f"a 512 MB L2 flush between timed steps (outside the step events); this GPU's shard "
+                      f"holds {idx.codes.numel() / 1e9:.2f} GB SQ8 codes + "
+                      f"{idx.storage.xb_sorted.numel() * 4 / 1e9:.2f} GB FP32 rows",
                 "parallelism": f"list-sharded x{d.world}" if d.world > 1 else "single GPU",
                 "phase_ms_per_step": {n: round(v / args.steps, 4) for n, v in phase_tot.items()},
                 "step_ms_min_max": [round(min(step_ms), 4), round(max(step_ms), 4)],

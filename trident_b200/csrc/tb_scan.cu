@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
 
     __shared__ int32_t s_qid[kMaxG], s_pp[kMaxG], s_seed[kMaxG];
     __shared__ float s_tau[kMaxG], s_ts[kMaxG], s_sig[kMaxG], s_scale[kMaxG], s_s2inv[kMaxG], s_tsp[kMaxG];
-    __shared__ int s_item, s_sn, s_lock[kMaxG];
+    __shared__ int s_item, s_sn, s_chunk, s_lock[kMaxG];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int K = a.K, D = a.D;
@@ -211,6 +211,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
         if (tid == 0) {
             s_item = atomicAdd(a.work_ctr, 1);
             s_sn = 0;
+            s_chunk = 0;
         }
         __syncthreads();
         const int it = s_item;
@@ -605,17 +606,24 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                 }
             };
 
-            for (int t = 0; t < nt; ++t) {
-                const int v = t * T + tid;
-                const bool valid = v < L;
-                const uint8_t* tp = codes_c + (size_t)t * nb * T * 32;
+            // The warps take the item's 32-row chunks in order as they become free, so a warp whose
+            // rows run deep takes fewer chunks (a chunk never crosses a tile: T is a multiple of 32).
+            const int nch = (L + 31) / 32;
+            for (;;) {
+                int ch = 0;
+                if (lane == 0) ch = atomicAdd(&s_chunk, 1);
+                ch = __shfl_sync(TB_FULL, ch, 0);
+                if (ch >= nch) break;
+                const int rb = ch * 32;  // first list-local row of the chunk
+                const bool valid = rb + lane < L;
+                const uint8_t* tp = codes_c + ((size_t)(rb / T) * nb * T + (rb % T)) * 32;
                 float cf[32];
                 uint4 p0 = make_uint4(0, 0, 0, 0), p1 = make_uint4(0, 0, 0, 0);
                 {
                     uint4 w0 = make_uint4(0, 0, 0, 0), w1 = make_uint4(0, 0, 0, 0);
                     if (valid) {
-                        load_block(tp + (size_t)tid * 32, w0, w1);
-                        if (nb > 1) load_block(tp + ((size_t)T + tid) * 32, p0, p1);
+                        load_block(tp + (size_t)lane * 32, w0, w1);
+                        if (nb > 1) load_block(tp + ((size_t)T + lane) * 32, p0, p1);
                     }
                     unpack_block(w0, w1, cf);
                 }
@@ -642,7 +650,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                     acc += a2.x + a2.y;
                     const bool alive = has && acc <= s_tsp[jj];
                     if (has) st_dims += 32u;
-                    const int row = t * T + warp * 32 + r;
+                    const int row = rb + r;
                     const unsigned m = __ballot_sync(TB_FULL, alive);
                     if (nb <= 2) {
                         unsigned dm = m;
@@ -693,7 +701,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                         while (dm) {
                             const int s = __ffs(dm) - 1;
                             dm &= dm - 1;
-                            refine_one(j, t * T + warp * 32 + s);
+                            refine_one(j, rb + s);
                         }
                         continue;
                     }
@@ -710,7 +718,7 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                         while (wq_n >= 32) deep_round(0);
                     }
                 }
-                // the tile's block-1 codes leave the registers: finish this warp's batch
+                // the chunk's block-1 codes leave the registers: finish this warp's batch
                 if (wcnt > 0) run_batch(wcnt);
                 while (wq_n >= 32) deep_round(0);
             }
