@@ -183,7 +183,7 @@ int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t
     if (B == 0) return TRIDENT_OK;
     cudaStream_t st = (cudaStream_t)stream;
     TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, st), "coarse_gemm");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, st), "coarse_gemm");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, probe_cids, probe_d64,
                                (unsigned long long*)stats, st),
            "probe_select");
@@ -224,7 +224,7 @@ static int search_impl(const trident_index* idx, const float* xq, int32_t B, int
     TB_TRY(mark(TRIDENT_PHASE_COARSE), "event");
     TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
     TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, st), "coarse_gemm");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, st), "coarse_gemm");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
     g_launches += 4;
 

@@ -128,64 +128,6 @@ cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, floa
 }
 
 // ------------------------------------------------------------------------------------------
-// Approximate coarse distances a[j][c] = ||c||^2 - 2 q_j.c (float32 SIMT GEMM, 64x64 tiles).
-// Any summation order satisfies the bound the selection uses: |a - exact| <= (D+2) u
-// (2||q|| Cmax + Cmax^2).
-// ------------------------------------------------------------------------------------------
-constexpr int kGM = 64, kGN = 64, kGK = 16;
-
-__global__ void __launch_bounds__(256) coarse_gemm_kernel(const float* __restrict__ xq, const float* __restrict__ cent,
-                                                         const float* __restrict__ cn, int B, int nlist, int D,
-                                                         float* __restrict__ out) {
-    __shared__ float sA[kGK][kGM + 4];
-    __shared__ float sB[kGK][kGN + 4];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    const int m0 = blockIdx.y * kGM, n0 = blockIdx.x * kGN;
-    float acc[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
-    for (int k0 = 0; k0 < D; k0 += kGK) {
-        for (int i = threadIdx.x; i < kGM * kGK; i += 256) {
-            const int r = i / kGK, k = i - r * kGK;
-            const int gm = m0 + r, gk = k0 + k;
-            sA[k][r] = (gm < B && gk < D) ? __ldg(xq + (int64_t)gm * D + gk) : 0.0f;
-            const int gn = n0 + r;
-            sB[k][r] = (gn < nlist && gk < D) ? __ldg(cent + (int64_t)gn * D + gk) : 0.0f;
-        }
-        __syncthreads();
-#pragma unroll
-        for (int k = 0; k < kGK; ++k) {
-            float a[4], b[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) { a[i] = sA[k][ty * 4 + i]; b[i] = sB[k][tx * 4 + i]; }
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int gm = m0 + ty * 4 + i;
-        if (gm >= B) continue;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int gn = n0 + tx * 4 + j;
-            if (gn < nlist) out[(int64_t)gm * nlist + gn] = cn[gn] - 2.0f * acc[i][j];
-        }
-    }
-}
-
-cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, cudaStream_t st) {
-    dim3 grid((idx.nlist + kGN - 1) / kGN, (B + kGM - 1) / kGM);
-    coarse_gemm_kernel<<<grid, 256, 0, st>>>(xq, idx.centroids, idx.centroid_norm_sq, B, idx.nlist, idx.D, coarse);
-    return cudaGetLastError();
-}
-
-// ------------------------------------------------------------------------------------------
 // Exact top-nprobe selection, one CTA per query.
 // ------------------------------------------------------------------------------------------
 constexpr int kSelThreads = 512;
@@ -284,7 +226,8 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
     const float* qi = qinfo + (int64_t)j * QI_LEN;
     const double qn = (double)qi[QI_QNORM];
     const double cm = (double)cmax;
-    const double E = (double)(D + 4) * u * 1.01 * (2.0 * qn * cm + cm * cm);
+    // error bound of the 3xTF32 tensor-core GEMM (tb_coarse_mma.cu)
+    const double E = ((double)(3 * D + 16) * 0x1p-22 + 3.02 * 0x1p-20) * 1.01 * (2.0 * qn * cm + cm * cm);
     const double eta = (double)(D + 2) * 2.220446049250313e-16 * (qn + cm) * (qn + cm);
     const float thr = __double2float_ru((double)t + 2.0 * E + 2.0 * eta);
 

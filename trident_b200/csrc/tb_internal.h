@@ -37,7 +37,9 @@ size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void*
 // Coarse stage (tb_coarse.cu).
 cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
                           uint32_t* tau, cudaStream_t st);
-cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, cudaStream_t st);
+// tcgen05 3xTF32 GEMM (tb_coarse_mma.cu); sets *err = 2 if a bounded wait gave up.
+cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, int32_t* err,
+                               cudaStream_t st);
 cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B, int nprobe, const float* coarse,
                                 const float* qinfo, int32_t* probe, double* probe_d64,
                                 unsigned long long* stats, cudaStream_t st);
