@@ -84,17 +84,15 @@ void oracle_topk_insert(float* d, int64_t* id, int K, float dv, int64_t iv) {
 }
 
 /* float64 direct squared distance: the oracle's definition of the coarse distance (the reference
- * fixes no float64 summation order; this one is chosen so that a warp evaluates it in parallel).
- * The D dims are cut into 32 contiguous chunks of C = ceil(D/32); chunk l sums fma(df, df, .) over
- * d in [l*C, min((l+1)*C, D)) in ascending d from 0.0; the 32 chunk sums are then added in order
- * l = 0..31. The GPU's exact re-check evaluates the same expression in the same order. */
+ * fixes no float64 summation order; this one is chosen so that a warp evaluates it in parallel
+ * with coalesced loads). Lane l in 0..31 sums fma(df, df, .) over d = l, l + 32, l + 64, ... < D
+ * in ascending d from 0.0; the 32 lane sums are then added in order l = 0..31. The GPU's exact
+ * re-check evaluates the same expression in the same order. */
 double oracle_l2_f64(const float* a, const float* b, int D) {
-    const int C = (D + 31) / 32;
     double total = 0.0;
     for (int l = 0; l < 32; ++l) {
         double acc = 0.0;
-        const int e = (l + 1) * C < D ? (l + 1) * C : D;
-        for (int d = l * C; d < e; ++d) {
+        for (int d = l; d < D; d += 32) {
             double df = (double)a[d] - (double)b[d];
             acc = fma(df, df, acc);
         }

@@ -25,50 +25,89 @@ namespace tb {
 
 // ------------------------------------------------------------------------------------------
 // Rotation: qrot[j][d] = float((q_j - mu) R[:, d]) with k ascending and fma (the oracle's
-// oracle_rotate_f64), as a register-tiled float64 GEMM: 64 queries x 64 dims per CTA, 16-deep
-// k-slices staged in shared memory, 4 x 4 outputs per thread. The k order of every output stays
-// sequential, so the result is bit-identical to the oracle.
+// oracle_rotate_f64), as a register-tiled float64 GEMM: 64 queries x 128 dims per CTA, 16-deep
+// k-slices, 4 x 8 outputs per thread. The next k-slice is loaded into registers while the current
+// one is multiplied from shared memory (two buffers), so global latency overlaps the DFMAs. The
+// k order of every output stays sequential, so the result is bit-identical to the oracle.
 // ------------------------------------------------------------------------------------------
 constexpr int kRM = 64, kRN = 128, kRK = 16;
 
 __global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict__ xq, const double* __restrict__ mu,
                                                         const double* __restrict__ R, int B, int D, int D_pad,
                                                         float* __restrict__ qrot) {
-    __shared__ __align__(16) double sQ[kRK][kRM];
-    __shared__ __align__(16) double sR[kRK][kRN];
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;  // rows ty*4..+3, columns tx + 16*j
+    __shared__ __align__(16) double sQ[2][kRK][kRM];
+    __shared__ __align__(16) double sR[2][kRK][kRN];
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;  // rows ty*4..+3, columns tx + 16*j
     const int m0 = blockIdx.x * kRM, n0 = blockIdx.y * kRN;
     double acc[4][8];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
-    for (int k0 = 0; k0 < D; k0 += kRK) {
-        const int kn = min(kRK, D - k0);
-        for (int i = threadIdx.x; i < kRM * kRK; i += 256) {
+    // staging assignment: 4 (row, k) elements of the query slice and 8 (k, column) of R per thread
+    double rq[4], rr[8];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int i = tid + 256 * t;
             const int r = i / kRK, k = i - r * kRK;
             const int gm = m0 + r, gk = k0 + k;
-            sQ[k][r] = (gm < B && k < kn) ? (double)__ldg(xq + (int64_t)gm * D + gk) - __ldg(mu + gk) : 0.0;
+            rq[t] = (gm < B && gk < D) ? (double)__ldg(xq + (int64_t)gm * D + gk) - __ldg(mu + gk) : 0.0;
         }
-        for (int i = threadIdx.x; i < kRK * kRN; i += 256) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int i = tid + 256 * t;
             const int k = i / kRN, n = i - k * kRN;
-            const int gn = n0 + n;
-            sR[k][n] = (k < kn && gn < D) ? __ldg(R + (int64_t)(k0 + k) * D + gn) : 0.0;
+            const int gk = k0 + k, gn = n0 + n;
+            rr[t] = (gk < D && gn < D) ? __ldg(R + (int64_t)gk * D + gn) : 0.0;
         }
-        __syncthreads();
-        for (int k = 0; k < kn; ++k) {
-            const double2 a01 = *reinterpret_cast<const double2*>(&sQ[k][ty * 4]);
-            const double2 a23 = *reinterpret_cast<const double2*>(&sQ[k][ty * 4 + 2]);
-            const double a[4] = {a01.x, a01.y, a23.x, a23.y};
-            double b[8];
+    };
+    auto stash = [&](int buf) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) b[j] = sR[k][tx + 16 * j];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+        for (int t = 0; t < 4; ++t) {
+            const int i = tid + 256 * t;
+            const int r = i / kRK, k = i - r * kRK;
+            sQ[buf][k][r] = rq[t];
         }
-        __syncthreads();
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const int i = tid + 256 * t;
+            const int k = i / kRN, n = i - k * kRN;
+            sR[buf][k][n] = rr[t];
+        }
+    };
+    auto step = [&](int buf, int k) {
+        const double2 a01 = *reinterpret_cast<const double2*>(&sQ[buf][k][ty * 4]);
+        const double2 a23 = *reinterpret_cast<const double2*>(&sQ[buf][k][ty * 4 + 2]);
+        const double a[4] = {a01.x, a01.y, a23.x, a23.y};
+        double b[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) b[j] = sR[buf][k][tx + 16 * j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
+    };
+    fetch(0);
+    stash(0);
+    __syncthreads();
+    int buf = 0;
+    for (int k0 = 0; k0 < D; k0 += kRK) {
+        const bool more = k0 + kRK < D;
+        if (more) fetch(k0 + kRK);  // in flight during this slice's DFMAs
+        const int kn = min(kRK, D - k0);
+        if (kn == kRK) {
+#pragma unroll
+            for (int k = 0; k < kRK; ++k) step(buf, k);
+        } else {
+            for (int k = 0; k < kn; ++k) step(buf, k);
+        }
+        if (more) {
+            stash(buf ^ 1);
+            __syncthreads();
+            buf ^= 1;
+        }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -168,15 +207,25 @@ __device__ __forceinline__ int block_sum_sel(int v, int* red) {
     return s;
 }
 
-// float64 ||q - c||^2 in the oracle's order (oracle_l2_f64): lane l sums its contiguous chunk of
-// C = ceil(D/32) dims with fma, then the 32 chunk sums are added in lane order. Every lane returns
-// the total.
+// float64 ||q - c||^2 in the oracle's order (oracle_l2_f64): lane l sums d = l, l + 32, ... with
+// fma (coalesced 128-byte loads of the centroid row), then the 32 lane sums are added in lane
+// order. Every lane returns the total.
 __device__ __forceinline__ double l2_f64_warp(const float* __restrict__ qv, const float* __restrict__ cr, int D,
                                               int lane) {
-    const int C = (D + 31) / 32;
-    const int d0 = lane * C, d1 = min(D, d0 + C);
     double acc = 0.0;
-    for (int d = d0; d < d1; ++d) {
+    int d = lane;
+    for (; d + 96 < D; d += 128) {  // four loads in flight, the same fma order
+        const float c0 = __ldg(cr + d), c1 = __ldg(cr + d + 32), c2 = __ldg(cr + d + 64), c3 = __ldg(cr + d + 96);
+        double df = (double)qv[d] - (double)c0;
+        acc = fma(df, df, acc);
+        df = (double)qv[d + 32] - (double)c1;
+        acc = fma(df, df, acc);
+        df = (double)qv[d + 64] - (double)c2;
+        acc = fma(df, df, acc);
+        df = (double)qv[d + 96] - (double)c3;
+        acc = fma(df, df, acc);
+    }
+    for (; d < D; d += 32) {
         const double df = (double)qv[d] - (double)__ldg(cr + d);
         acc = fma(df, df, acc);
     }
@@ -222,7 +271,6 @@ __global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
     const float t = key_float(ans);
 
     // 2) members: approximate value within the certified band above t
-    const double u = 5.9604644775390625e-08;
     const float* qi = qinfo + (int64_t)j * QI_LEN;
     const double qn = (double)qi[QI_QNORM];
     const double cm = (double)cmax;

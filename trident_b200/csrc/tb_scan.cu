@@ -293,7 +293,10 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                             id = __ldg(a.oid + r0 + entry_r(e));
                         }
                     }
-                    if (__any_sync(TB_FULL, ok)) st_ins += (unsigned)list_offer<KM>(ld, li, K, ok, d, id, lane);
+                    if (__any_sync(TB_FULL, ok)) {
+                        const int ins = list_offer<KM>(ld, li, K, ok, d, id, lane);
+                        if (lane == 0) st_ins += (unsigned)ins;
+                    }
                 }
                 if (lane == 0) {
                     const float kth = ld[K - 1];
@@ -513,7 +516,8 @@ __global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
                 __threadfence_block();
                 float* ld = s_topd + j * KM;
                 int32_t* li = s_topi + j * KM;
-                st_ins += (unsigned)list_offer<KM>(ld, li, K, lane == 0, dist, id, lane);
+                const int ins = list_offer<KM>(ld, li, K, lane == 0, dist, id, lane);
+                if (lane == 0) st_ins += (unsigned)ins;
                 if (lane == 0) {
                     st_surv += 1;
                     const float kth = ld[K - 1];
