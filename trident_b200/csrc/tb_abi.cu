@@ -82,6 +82,8 @@ size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void*
     w.pair_q = (int32_t*)take(pairs * sizeof(int32_t));
     w.pair_p = (int32_t*)take(pairs * sizeof(int32_t));
     w.items = (int4*)take(pairs * sizeof(int4));
+    w.items_lpt = (int4*)take(pairs * sizeof(int4));
+    w.lpt = (int32_t*)take(kLptBins * sizeof(int32_t));
     w.tau = (uint32_t*)take(Bs * sizeof(uint32_t));
     w.cand_d = (float*)take(pairs * (size_t)K * sizeof(float));
     w.cand_i = (int32_t*)take(pairs * (size_t)K * sizeof(int32_t));
@@ -233,7 +235,8 @@ static int search_impl(const trident_index* idx, const float* xq, int32_t B, int
     const int G = scan_group_size(*idx, K);
     TB_TRY(mark(TRIDENT_PHASE_PAIRS), "event");
     TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, 0, G, K, ws, st), "pairs");
-    g_launches += 4;
+    TB_TRY(launch_item_order(*idx, B * nprobe, ws, st), "item order");
+    g_launches += 7;
     if (lb) {
         TB_TRY(mark(TRIDENT_PHASE_SEED), "event");
         TB_TRY(launch_seed(*idx, xq, ws, B, K, nprobe, seed_lists_for(B, K, nprobe), ub_seed >= 1, st), "seed");

@@ -24,7 +24,9 @@ struct Workspace {
     int32_t* item_off;  // [2, nlist + 1]
     int32_t* pair_q;    // [B * nprobe]
     int32_t* pair_p;    // [B * nprobe]
-    int4* items;        // [B * nprobe]
+    int4* items;        // [B * nprobe] in list order
+    int4* items_lpt;    // [B * nprobe] the same items, most expensive first
+    int32_t* lpt;       // [kLptBins] bin counts, then bin cursors
     uint32_t* tau;      // [B] float bits of each query's current K-th distance
     float* cand_d;      // [B, nprobe, K]
     int32_t* cand_i;    // [B, nprobe, K]
@@ -47,6 +49,10 @@ cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B
 // Pair lists and work items (tb_pairs.cu).
 cudaError_t launch_pairs(const trident_index& idx, const int32_t* probe, int B, int nprobe, int p_init, int G, int K,
                          const Workspace& ws, cudaStream_t st);
+constexpr int kLptBins = 128;
+// Reorders the main pass's items by estimated cost, largest first (longest-processing-time order),
+// into ws.items_lpt.
+cudaError_t launch_item_order(const trident_index& idx, int max_items, const Workspace& ws, cudaStream_t st);
 
 // Query-major threshold seeding (tb_seed.cu): rank the rows of each query's p_seed nearest lists by
 // a partial SQ8 distance, refine the best exactly (or bound them from above with ub) and store the

@@ -142,4 +142,65 @@ cudaError_t launch_pairs(const trident_index& idx, const int32_t* probe, int B, 
     return cudaGetLastError();
 }
 
+// ---- longest-processing-time order of the main pass's items. The scan is a persistent kernel that
+// takes items from a counter; handing out the expensive items first keeps the last CTAs from
+// finishing a big item alone. Cost estimate: (rows + 32) x (queries + 2); bin = 4 log2(cost),
+// reversed so that bin 0 is the most expensive. The order inside a bin is arbitrary (atomics);
+// results do not depend on it.
+__device__ __forceinline__ int lpt_bin(const int4 it, const int64_t* __restrict__ row_off) {
+    const unsigned long long L = (unsigned long long)(row_off[it.x + 1] - row_off[it.x]);
+    const unsigned long long cost = (L + 32ull) * (unsigned long long)(it.z + 2);
+    const int msb = 63 - __clzll((long long)cost);
+    const int frac = msb >= 2 ? (int)((cost >> (msb - 2)) & 3ull) : 0;
+    const int key = min(kLptBins - 1, 4 * msb + frac);
+    return kLptBins - 1 - key;
+}
+
+__global__ void lpt_hist_kernel(const int4* __restrict__ items, const int32_t* __restrict__ n_items,
+                                const int64_t* __restrict__ row_off, int32_t* __restrict__ hist) {
+    const int n = *n_items;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+        atomicAdd(&hist[lpt_bin(items[i], row_off)], 1);
+}
+
+__global__ void __launch_bounds__(kLptBins) lpt_scan_kernel(int32_t* __restrict__ hist) {
+    __shared__ int32_t s[kLptBins];
+    const int t = threadIdx.x;
+    s[t] = hist[t];
+    __syncthreads();
+    if (t == 0) {
+        int run = 0;
+        for (int b = 0; b < kLptBins; ++b) {
+            const int c = s[b];
+            s[b] = run;
+            run += c;
+        }
+    }
+    __syncthreads();
+    hist[t] = s[t];  // now the cursor of each bin
+}
+
+__global__ void lpt_scatter_kernel(const int4* __restrict__ items, const int32_t* __restrict__ n_items,
+                                   const int64_t* __restrict__ row_off, int32_t* __restrict__ cursor,
+                                   int4* __restrict__ out) {
+    const int n = *n_items;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const int4 it = items[i];
+        out[atomicAdd(&cursor[lpt_bin(it, row_off)], 1)] = it;
+    }
+}
+
+cudaError_t launch_item_order(const trident_index& idx, int max_items, const Workspace& ws, cudaStream_t st) {
+    if (max_items <= 0) return cudaSuccess;
+    cudaError_t e = cudaMemsetAsync(ws.lpt, 0, kLptBins * sizeof(int32_t), st);
+    if (e != cudaSuccess) return e;
+    int blocks = (max_items + 255) / 256;
+    const int cap = num_sms() * 4;
+    if (blocks > cap) blocks = cap;
+    lpt_hist_kernel<<<blocks, 256, 0, st>>>(ws.items, ws.ctr + 1, idx.list_row_off, ws.lpt);
+    lpt_scan_kernel<<<1, kLptBins, 0, st>>>(ws.lpt);
+    lpt_scatter_kernel<<<blocks, 256, 0, st>>>(ws.items, ws.ctr + 1, idx.list_row_off, ws.lpt, ws.items_lpt);
+    return cudaGetLastError();
+}
+
 }  // namespace tb

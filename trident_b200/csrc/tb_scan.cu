@@ -47,7 +47,9 @@ struct ScanArgs {
     float rho;
 };
 
-constexpr int kMaxG = 32;
+constexpr int kMaxG = 64;
+// Resident scan threads per SM the kernel is compiled for (registers) and sized for (shared memory).
+constexpr int kScanThreadsPerSm = 512;
 
 // Stage Y on one 32-dim block: acc += sum_d max(|code_d delta_d + (vmin_d - q~_d)| - eps_d, 0)^2
 // (reference :750-767). base/dl/ep point at the block's 32 entries in shared memory.
@@ -168,13 +170,14 @@ constexpr int kGC = 4;   // queries per CM-FP32 chunk: a chunk adds at most kGC 
 constexpr int kQM = 4;   // survivor-list capacity in units of T entries (>= kGC, >= the seed count)
 constexpr int kNBR = 1;  // code blocks a lane loads per deep-queue round (2 and 4 measured slower)
 
-// Survivor / deep-queue entry: query slot j (5 bits) and list-local row r (27 bits).
-__device__ __forceinline__ uint32_t pack_jr(int j, int r) { return ((uint32_t)j << 27) | (uint32_t)r; }
-__device__ __forceinline__ int entry_j(uint32_t e) { return (int)(e >> 27); }
-__device__ __forceinline__ int entry_r(uint32_t e) { return (int)(e & 0x7FFFFFFu); }
+// Survivor / deep-queue entry: query slot j (kJBits bits) and list-local row r (the rest).
+constexpr int kJBits = kMaxG <= 32 ? 5 : 6;
+__device__ __forceinline__ uint32_t pack_jr(int j, int r) { return ((uint32_t)j << (32 - kJBits)) | (uint32_t)r; }
+__device__ __forceinline__ int entry_j(uint32_t e) { return (int)(e >> (32 - kJBits)); }
+__device__ __forceinline__ int entry_r(uint32_t e) { return (int)(e & ((1u << (32 - kJBits)) - 1u)); }
 
 template <int T, int KM, bool LB, bool UB, bool VEC4>
-__global__ void __launch_bounds__(T, 512 / T) scan_kernel(const ScanArgs a) {
+__global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const ScanArgs a) {
     constexpr int NW = T / 32;
     constexpr int QCAP = kQM * T;
     extern __shared__ __align__(16) unsigned char smem[];
@@ -874,8 +877,10 @@ static size_t scan_smem(const trident_index& idx, int K, int G, bool lb) {
 }
 
 int scan_group_size(const trident_index& idx, int K) {
-    // Two CTAs of 256 rows (or four of 128) per SM: about 100 KB of shared memory each.
-    const size_t budget = (idx.tile_size == 256) ? 100 * 1024 : 50 * 1024;
+    // kScanThreadsPerSm / T CTAs share an SM's 228 KB; 4 KB per CTA stay for static shared memory and
+    // the per-CTA reserve.
+    const size_t ctas = (size_t)(kScanThreadsPerSm / idx.tile_size);
+    const size_t budget = (228 * 1024) / ctas - 4 * 1024;
     int G = kMaxG;
     while (G > 1 && scan_smem(idx, K, G, true) > budget) --G;
     return G;
@@ -926,7 +931,7 @@ cudaError_t launch_scan(const trident_index& idx, const float* xq, const Workspa
     a.xq = xq;
     a.qrot = ws.qrot;
     a.qinfo = ws.qinfo;
-    a.items = ws.items + sl.item_base;
+    a.items = (sl.pass == 1 ? ws.items_lpt : ws.items) + (sl.pass == 1 ? 0 : sl.item_base);
     a.n_items = ws.ctr + sl.pass;
     a.work_ctr = ws.ctr + 2 + sl.pass;
     a.pair_q = ws.pair_q;

@@ -59,24 +59,30 @@ class ShardedSearch:
     merges them on the device.
     """
 
-    def __init__(self, index, group=None):
+    def __init__(self, index, group=None, merge=None):
         import torch.distributed as dist
 
         self.index = index
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
+        self.merge = merge  # (d_all [R,B,K], i_all [R,B,K]) -> (d, i); None: the device merge
 
     def search(self, xq_gpu, nprobe: int, k: int = 10, mode: int = 2, ub_seed: int = 0, phase_ms=None):
         import torch
         import torch.distributed as dist
 
-        from .index import merge_shards
-
         d_loc, i_loc, _ = self.index.search(xq_gpu, nprobe, mode=mode, k=k, ub_seed=ub_seed, phase_ms=phase_ms)
         B = d_loc.shape[0]
-        d_all = torch.empty((self.world, B, k), dtype=torch.float32, device=d_loc.device)
-        i_all = torch.empty((self.world, B, k), dtype=torch.int64, device=d_loc.device)
+        # rank-major [R * B, K] (the shape every backend accepts), viewed as [R, B, K]
+        d_all = torch.empty((self.world * B, k), dtype=torch.float32, device=d_loc.device)
+        i_all = torch.empty((self.world * B, k), dtype=torch.int64, device=d_loc.device)
         dist.all_gather_into_tensor(d_all, d_loc.contiguous(), group=self.group)
         dist.all_gather_into_tensor(i_all, i_loc.contiguous(), group=self.group)
+        d_all = d_all.view(self.world, B, k)
+        i_all = i_all.view(self.world, B, k)
+        if self.merge is not None:
+            return self.merge(d_all, i_all)
+        from .index import merge_shards
+
         return merge_shards(d_all, i_all)
