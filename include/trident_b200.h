@@ -179,6 +179,41 @@ int trident_search_noalloc(const trident_index* idx, const float* xq, int32_t B,
                            int32_t mode, int32_t ub_seed, float* out_d, int64_t* out_i, int64_t* stats,
                            void* stream);
 
+/* Per-query side information of trident_search_prep: [B, TRIDENT_QINFO_LEN] float32 (||q||,
+ * the bound's query slack sigma, ||q - mu||, padding). */
+#define TRIDENT_QINFO_LEN 4
+
+/* The search in three stages, for list sharding over GPUs (one process per GPU; no counterpart
+ * in the reference, which ran on one GPU). Every rank's index holds all centroids and only the
+ * rows of its own lists. A batch of B_all queries, B_r of them owned by rank r, is processed as
+ * follows:
+ *   1. trident_search_prep on the rank's own B_r queries writes their probe lists
+ *      [B_r, nprobe], rotated queries [B_r, D_pad] and qinfo [B_r, TRIDENT_QINFO_LEN];
+ *   2. the caller all-gathers those and the query vectors into [B_all, ...];
+ *   3. trident_search_seed on the whole batch builds the work items for the local lists and
+ *      writes each query's K smallest seed values of the local rows, with their row ids, into
+ *      seed_d [B_all, K] and seed_i [B_all, K], ascending and padded with (+inf, -1). A GPU
+ *      refines a share of the seed rows proportional to the seed lists it holds;
+ *   4. the caller gathers the R seed lists, merges them with trident_merge_shards and takes
+ *      column K-1 as tau [B_all]. That is the K-th smallest over the distinct rows of all
+ *      ranks, so it bounds the final K-th distance;
+ *   5. trident_search_finish scans the local lists with those thresholds and writes the
+ *      per-query top-K of the local rows, [B_all, K];
+ *   6. the caller gathers the R lists and merges them with trident_merge_shards.
+ * Steps 3 and 5 must use the same workspace, sized for (B_all, K, nprobe), and the same
+ * mode/ub_seed/K/nprobe. A single GPU runs the same stages inside trident_search. */
+int trident_search_prep(const trident_index* idx, const float* xq, int32_t B, int32_t nprobe,
+                        void* workspace, size_t workspace_bytes, int32_t* probe_out, float* qrot_out,
+                        float* qinfo_out, void* stream);
+int trident_search_seed(const trident_index* idx, const float* xq_all, int32_t B_all, int32_t K,
+                        int32_t nprobe, int32_t mode, int32_t ub_seed, const int32_t* probe,
+                        const float* qrot, const float* qinfo, void* workspace, size_t workspace_bytes,
+                        float* seed_d, int64_t* seed_i, void* stream);
+int trident_search_finish(const trident_index* idx, const float* xq_all, int32_t B_all, int32_t K,
+                          int32_t nprobe, int32_t mode, int32_t ub_seed, const float* tau_in,
+                          void* workspace, size_t workspace_bytes, float* out_d, int64_t* out_i,
+                          int64_t* stats, void* stream);
+
 /* Multi-GPU merge: R per-shard result lists d_in/i_in [R, B, K] (as gathered by an NCCL
  * all-gather) -> the global top-K per query under the (distance, id) order. */
 int trident_merge_shards(const float* d_in, const int64_t* i_in, int32_t R, int32_t B, int32_t K,

@@ -217,6 +217,65 @@ def test_list_sharding_on_one_gpu(cases):
     assert_same_topk(gd.cpu().numpy(), gi.cpu().numpy(), od, oi)
 
 
+def _shard_indexes(f, R, tile_size=128):
+    torch = _torch()
+    from trident_b200 import SharedClusterStorage, TridentV4Index
+    from trident_b200.shard import partition_lists, shard_rows
+
+    counts = np.bincount(f["list_ids"], minlength=int(f["nlist"]))
+    owner = partition_lists(counts, R)
+    out = []
+    for r in range(R):
+        rows = shard_rows(f["list_ids"], owner, r)
+        st = SharedClusterStorage(f["xb"][rows], f["list_ids"][rows], None, int(f["nlist"]), device="cuda:0")
+        st.orig_ids_sorted = torch.from_numpy(rows.astype(np.int32)).cuda()[st.orig_ids_sorted.long()].contiguous()
+        out.append(TridentV4Index(st, f["centroids"], f["mean64"], f["R64"], tile_size=tile_size, device="cuda:0"))
+    return out
+
+
+@pytest.mark.parametrize("mode", [2, 10])
+def test_staged_search_equals_one_call(cases, mode):
+    """prep -> seed -> finish on one index gives trident_search's result bit for bit."""
+    torch = _torch()
+    f = cases["g2_decay_c2"]
+    idx, nprobe, K = f["index"], int(f["nprobe"]), int(f["K"])
+    xq = torch.from_numpy(f["xq"]).cuda()
+    d0, i0 = _search(idx, f["xq"], nprobe, K, mode=mode)
+    probe, qrot, qinfo = idx.search_prep(xq, nprobe)
+    seed_d, _ = idx.search_seed(xq, probe, qrot, qinfo, nprobe, k=K, mode=mode)
+    d, i = idx.search_finish(xq, seed_d[:, K - 1].contiguous(), nprobe, k=K, mode=mode)
+    torch.cuda.synchronize()
+    assert np.array_equal(i.cpu().numpy(), i0) and np.array_equal(d.cpu().numpy(), d0)
+
+
+@pytest.mark.parametrize("ub", [0, 1])
+def test_staged_sharding_on_one_gpu(cases, ub):
+    """The multi-GPU protocol of ShardedSearch, emulated on one GPU with R = 3 shard indexes: each
+    shard owns a slice of the queries. The protocol is: prep on the owner, gather, seed on every
+    shard, merge of the seed lists into thresholds, finish on every shard, then the all-to-all and
+    merge. The result must equal the unsharded oracle."""
+    torch = _torch()
+    from trident_b200 import merge_shards
+
+    f = cases["g3_norm_c3"]
+    R, nprobe, K = 3, int(f["nprobe"]), int(f["K"])
+    shards = _shard_indexes(f, R)
+    B = f["xq"].shape[0] // R
+    xq_all = torch.from_numpy(np.ascontiguousarray(f["xq"][:R * B])).cuda()
+    parts = [shards[r].search_prep(xq_all[r * B:(r + 1) * B].contiguous(), nprobe) for r in range(R)]
+    probe, qrot, qinfo = (torch.cat([p[k] for p in parts]).contiguous() for k in range(3))
+    seeds = [s.search_seed(xq_all, probe, qrot, qinfo, nprobe, k=K, mode=2, ub_seed=ub) for s in shards]
+    sd, _ = merge_shards(torch.stack([x[0] for x in seeds]).contiguous(), torch.stack([x[1] for x in seeds]).contiguous())
+    tau = sd[:, K - 1].contiguous()
+    outs = [s.search_finish(xq_all, tau, nprobe, k=K, mode=2, ub_seed=ub) for s in shards]
+    od, oi, _ = _oracle(f, xq=f["xq"][:R * B])
+    for r in range(R):
+        d_in = torch.stack([o[0][r * B:(r + 1) * B] for o in outs]).contiguous()
+        i_in = torch.stack([o[1][r * B:(r + 1) * B] for o in outs]).contiguous()
+        gd, gi = merge_shards(d_in, i_in)
+        assert_same_topk(gd.cpu().numpy(), gi.cpu().numpy(), od[r * B:(r + 1) * B], oi[r * B:(r + 1) * B])
+
+
 @pytest.mark.parametrize("cfg_name,overrides,modes", [
     ("c1", {}, (2, 10)),                                                   # configs[0] at full size
     ("c2", dict(N=100_000, nlist=128, nprobe=8, B=200), (2,)),             # C2 rows, smaller N

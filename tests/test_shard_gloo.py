@@ -1,9 +1,13 @@
 """List sharding across two processes with the gloo backend, on the CPU.
 
-Each rank owns the lists `partition_lists` gives it and holds only their rows, selects the same
-probe set from all centroids, searches its own rows (the CPU oracle stands in for the GPU index
-here) and takes part in the all-gather of `ShardedSearch`. The merged top-K must equal the
-unsharded oracle's. The bench runs the same protocol over NCCL with one GPU per rank.
+Each rank owns the lists `partition_lists` gives it and holds only their rows, and brings its own
+half of the queries. ShardedSearch then runs the staged protocol:
+  - all-gather of the probe lists and queries;
+  - threshold seed lists, gathered and merged into each query's threshold;
+  - local scan, where nothing above the threshold is emitted;
+  - all-to-all and merge.
+The CPU oracle stands in for the GPU stages. Every rank's merged top-K must equal the unsharded
+oracle's for its own queries. The bench runs the same protocol over NCCL with one GPU per rank.
 """
 import os
 import socket
@@ -22,7 +26,7 @@ def _free_port():
 
 
 class _OracleShard:
-    """This rank's rows behind the search() signature of TridentV4Index (CPU oracle)."""
+    """This rank's rows behind the staged-search methods of TridentV4Index (CPU oracle)."""
 
     def __init__(self, f, owner, rank):
         nlist = int(f["nlist"])
@@ -34,16 +38,44 @@ class _OracleShard:
         self.xs = np.ascontiguousarray(xs[keep])
         self.perm = np.ascontiguousarray(perm[keep])
         self.centroids = f["centroids"]
+        self.D_pad = (f["xb"].shape[1] + 31) // 32 * 32
 
-    def search(self, xq, nprobe, mode=2, k=10, ub_seed=0, phase_ms=None):
+    def _local(self, xq, probe, k):
+        from oracle import oracle as O
+
+        return O.ivf_search(xq.numpy(), np.ascontiguousarray(probe.numpy()), self.off, self.xs, self.perm, k)
+
+    def search_prep(self, xq, nprobe):
         import torch
 
         from oracle import oracle as O
 
-        xq = xq.numpy()
-        cids, _ = O.probe_select_f64(xq, self.centroids, nprobe)
-        d, i = O.ivf_search(xq, cids, self.off, self.xs, self.perm, k)
-        return torch.from_numpy(np.ascontiguousarray(d)), torch.from_numpy(np.ascontiguousarray(i).astype(np.int64)), 0.0
+        cids, _ = O.probe_select_f64(xq.numpy(), self.centroids, nprobe)
+        B = xq.shape[0]
+        return (torch.from_numpy(np.ascontiguousarray(cids).astype(np.int32)),
+                torch.zeros((B, self.D_pad), dtype=torch.float32), torch.zeros((B, 4), dtype=torch.float32))
+
+    def search_seed(self, xq_all, probe, qrot, qinfo, nprobe, k=10, mode=2, ub_seed=0):
+        import torch
+
+        d, i = self._local(xq_all, probe, k)  # exact distances of distinct local rows
+        return torch.from_numpy(np.ascontiguousarray(d)), torch.from_numpy(np.ascontiguousarray(i).astype(np.int64))
+
+    def search_finish(self, xq_all, tau, nprobe, k=10, mode=2, ub_seed=0):
+        import torch
+
+        probe = torch.from_numpy(np.ascontiguousarray(self._probe_all(xq_all, nprobe)))
+        d, i = self._local(xq_all, probe, k)
+        drop = d > tau.numpy()[:, None]  # what the scan emits: nothing above the threshold
+        d, i = d.copy(), i.astype(np.int64)
+        d[drop], i[drop] = np.inf, -1
+        return torch.from_numpy(d), torch.from_numpy(i)
+
+    def _probe_all(self, xq_all, nprobe):
+        from oracle import oracle as O
+
+        cids, _ = O.probe_select_f64(xq_all.numpy(), self.centroids, nprobe)
+        return cids.astype(np.int32)
 
 
 def _merge_host(d_all, i_all):
@@ -68,9 +100,10 @@ def _rank(rank, world, port, name, K, out_path):
         counts = np.bincount(f["list_ids"], minlength=int(f["nlist"]))
         owner = partition_lists(counts, world)
         ss = ShardedSearch(_OracleShard(f, owner, rank), merge=_merge_host)
-        d, i = ss.search(torch.from_numpy(f["xq"]), int(f["nprobe"]), k=K)
-        if rank == 0:
-            np.savez(out_path, d=d.numpy(), i=i.numpy())
+        xq = f["xq"]
+        B = xq.shape[0] // world  # every rank brings its own slice of the queries
+        d, i = ss.search(torch.from_numpy(np.ascontiguousarray(xq[rank * B:(rank + 1) * B])), int(f["nprobe"]), k=K)
+        np.savez(out_path + f".{rank}.npz", d=d.numpy(), i=i.numpy())
     finally:
         dist.destroy_process_group()
 
@@ -79,12 +112,13 @@ def _rank(rank, world, port, name, K, out_path):
 def test_two_rank_list_sharding_matches_unsharded(tmp_path, name, K):
     import torch.multiprocessing as mp
 
-    out = str(tmp_path / "merged.npz")
+    out = str(tmp_path / "merged")
     mp.start_processes(_rank, args=(2, _free_port(), name, K, out), nprocs=2, join=True, start_method="spawn")
-    got = np.load(out)
+    parts = [np.load(out + f".{r}.npz") for r in range(2)]
     f = load_case(name)
-    od, oi, _ = oracle_search(f["xb"], f["list_ids"], f["centroids"], f["xq"], int(f["nprobe"]), K)
-    assert_same_topk(got["d"], got["i"], od, oi)
+    B = f["xq"].shape[0] // 2
+    od, oi, _ = oracle_search(f["xb"], f["list_ids"], f["centroids"], f["xq"][:2 * B], int(f["nprobe"]), K)
+    assert_same_topk(np.concatenate([p["d"] for p in parts]), np.concatenate([p["i"] for p in parts]), od, oi)
 
 
 def test_partition_is_balanced_and_total():

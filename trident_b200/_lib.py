@@ -25,8 +25,10 @@ STAT_NAMES = ("candidates", "scanned_dims", "survivors", "inserted", "coarse_rec
 EXPORTED = (
     "trident_version", "trident_last_error", "trident_index_check", "trident_workspace_size", "trident_p_init",
     "trident_route", "trident_search", "trident_search_profiled", "trident_launch_count", "trident_coarse",
-    "trident_merge_shards", "trident_search_noalloc",
+    "trident_merge_shards", "trident_search_noalloc", "trident_search_prep", "trident_search_seed",
+    "trident_search_finish",
 )
+QINFO_LEN = 4
 NOALLOC_WORKSPACE_BYTES = 32 * 1024 * 1024
 PHASES = ("coarse", "pairs", "seed", "scan", "merge")
 
@@ -92,8 +94,12 @@ def lib():
     L.trident_coarse.argtypes = [DP, P, i32, i32, P, sz, P, P, P, P, P]
     L.trident_merge_shards.argtypes = [P, P, i32, i32, i32, P, P, P]
     L.trident_search_noalloc.argtypes = [DP, P, i32, i32, i32, i32, i32, P, P, P, P]
+    L.trident_search_prep.argtypes = [DP, P, i32, i32, P, sz, P, P, P, P]
+    L.trident_search_seed.argtypes = [DP, P, i32, i32, i32, i32, i32, P, P, P, P, sz, P, P, P]
+    L.trident_search_finish.argtypes = [DP, P, i32, i32, i32, i32, i32, P, P, sz, P, P, P, P]
     for name in ("trident_index_check", "trident_workspace_size", "trident_search", "trident_search_profiled",
-                 "trident_coarse", "trident_merge_shards", "trident_search_noalloc"):
+                 "trident_coarse", "trident_merge_shards", "trident_search_noalloc", "trident_search_prep",
+                 "trident_search_seed", "trident_search_finish"):
         getattr(L, name).restype = ctypes.c_int
     _LIB = L
     return L

@@ -45,6 +45,8 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 namespace tb {
 
+static_assert(QI_LEN == TRIDENT_QINFO_LEN, "qinfo layout");
+
 int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
 int num_sms() {
@@ -203,35 +205,33 @@ struct PhaseEvents {
     bool on = false;
 };
 
-static int search_impl(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, int32_t mode,
-                       int32_t ub_seed, void* workspace, size_t workspace_bytes, float* out_d, int64_t* out_i,
-                       int64_t* stats, cudaStream_t st, PhaseEvents* pe) {
-    Workspace ws;
-    int rc = check_search_args(idx, xq, B, K, nprobe, workspace, workspace_bytes, &ws);
-    if (rc) return rc;
-    if (B > 0 && (!out_d || !out_i)) return fail(TRIDENT_ERR_INVALID, "out_d / out_i is NULL");
-    if (ub_seed < 0 || ub_seed > 2) return fail(TRIDENT_ERR_INVALID, "ub_seed=%d outside [0, 2]", ub_seed);
-    if (mode == TRIDENT_MODE_AUTO) mode = trident_route(idx, B, nprobe, 0.0);
-    if (mode != TRIDENT_MODE_CASCADE && mode != TRIDENT_MODE_CM_FP32)
-        return fail(TRIDENT_ERR_UNSUPPORTED, "mode=%d (supported: -1 auto, 2 cascade, 10 CM-FP32)", mode);
-    if (B == 0) return TRIDENT_OK;
-    unsigned long long* sp = (unsigned long long*)stats;
-    const bool lb = mode == TRIDENT_MODE_CASCADE;
-    auto mark = [&](int phase) -> cudaError_t {  // event at the start of `phase` (or the end, PHASES)
+// Records the CUDA event at the start of a phase (or the end, TRIDENT_PHASES) of a profiled call.
+struct Marker {
+    PhaseEvents* pe;
+    cudaStream_t st;
+    cudaError_t operator()(int phase) const {
         if (!pe) return cudaSuccess;
         if (phase < TRIDENT_PHASES) pe->ran[phase] = true;
         return cudaEventRecord(pe->ev[phase], st);
-    };
+    }
+};
 
-    TB_TRY(mark(TRIDENT_PHASE_COARSE), "event");
-    TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
+// Stage 1 of a search: rotation, coarse GEMM and exact probe selection for B queries, into ws.
+static int stage_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t nprobe, const Workspace& ws,
+                        unsigned long long* sp, cudaStream_t st) {
     TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
     TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, st), "coarse_gemm");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
     g_launches += 4;
+    return TRIDENT_OK;
+}
 
-    // One pass over every probe. The reference scans its p_init warm-up lists first to obtain the
-    // thresholds; here the query-major seed kernel takes that role before the scan starts.
+// Stage 2: cluster-major work items over every probe with rows, then (cascade) the Stage X seed.
+// One pass covers every probe: the reference scans its p_init warm-up lists first to obtain the
+// thresholds, here the query-major seed kernel takes that role before the scan starts.
+static int stage_seed(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, bool lb,
+                      int32_t ub_seed, const Workspace& ws, cudaStream_t st, const Marker& mark,
+                      float* seed_d = nullptr, int64_t* seed_i = nullptr) {
     const int G = scan_group_size(*idx, K);
     TB_TRY(mark(TRIDENT_PHASE_PAIRS), "event");
     TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, 0, G, K, ws, st), "pairs");
@@ -239,23 +239,60 @@ static int search_impl(const trident_index* idx, const float* xq, int32_t B, int
     g_launches += 7;
     if (lb) {
         TB_TRY(mark(TRIDENT_PHASE_SEED), "event");
-        TB_TRY(launch_seed(*idx, xq, ws, B, K, nprobe, seed_lists_for(B, K, nprobe), ub_seed >= 1, st), "seed");
+        TB_TRY(launch_seed(*idx, xq, ws, B, K, nprobe, seed_lists_for(B, K, nprobe), ub_seed >= 1, seed_d, seed_i,
+                           seed_d != nullptr, st),
+               "seed");
         g_launches += 1;
     }
+    return TRIDENT_OK;
+}
+
+// Stage 3: Stage Y/Z (or CM-FP32) over the items, then the per-query merge into the output.
+static int stage_scan(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, bool lb,
+                      int32_t ub_seed, const Workspace& ws, float* out_d, int64_t* out_i, unsigned long long* sp,
+                      cudaStream_t st, const Marker& mark) {
     ScanLaunch sl;
     sl.K = K;
     sl.nprobe = nprobe;
-    sl.G = G;
+    sl.G = scan_group_size(*idx, K);
     sl.lb = lb ? 1 : 0;
     sl.pass = 1;
     sl.ub_seed = (lb && ub_seed == 2) ? 1 : 0;
     sl.max_items = B * nprobe;
     sl.item_base = 0;
     TB_TRY(mark(TRIDENT_PHASE_SCAN), "event");
-    TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan pass 1");
+    TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan");
     TB_TRY(mark(TRIDENT_PHASE_MERGE), "event");
     TB_TRY(launch_merge(ws, B, K, nprobe, 0, nprobe, nullptr, out_d, out_i, st), "merge");
     g_launches += 2;
+    return TRIDENT_OK;
+}
+
+static int resolve_mode(const trident_index* idx, int32_t B, int32_t nprobe, int32_t* mode, int32_t ub_seed) {
+    if (ub_seed < 0 || ub_seed > 2) return fail(TRIDENT_ERR_INVALID, "ub_seed=%d outside [0, 2]", ub_seed);
+    if (*mode == TRIDENT_MODE_AUTO) *mode = trident_route(idx, B, nprobe, 0.0);
+    if (*mode != TRIDENT_MODE_CASCADE && *mode != TRIDENT_MODE_CM_FP32)
+        return fail(TRIDENT_ERR_UNSUPPORTED, "mode=%d (supported: -1 auto, 2 cascade, 10 CM-FP32)", *mode);
+    return TRIDENT_OK;
+}
+
+static int search_impl(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, int32_t mode,
+                       int32_t ub_seed, void* workspace, size_t workspace_bytes, float* out_d, int64_t* out_i,
+                       int64_t* stats, cudaStream_t st, PhaseEvents* pe) {
+    Workspace ws;
+    int rc = check_search_args(idx, xq, B, K, nprobe, workspace, workspace_bytes, &ws);
+    if (rc) return rc;
+    if (B > 0 && (!out_d || !out_i)) return fail(TRIDENT_ERR_INVALID, "out_d / out_i is NULL");
+    if ((rc = resolve_mode(idx, B, nprobe, &mode, ub_seed))) return rc;
+    if (B == 0) return TRIDENT_OK;
+    unsigned long long* sp = (unsigned long long*)stats;
+    const bool lb = mode == TRIDENT_MODE_CASCADE;
+    const Marker mark{pe, st};
+    TB_TRY(mark(TRIDENT_PHASE_COARSE), "event");
+    TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
+    if ((rc = stage_coarse(idx, xq, B, nprobe, ws, sp, st))) return rc;
+    if ((rc = stage_seed(idx, xq, B, K, nprobe, lb, ub_seed, ws, st, mark))) return rc;
+    if ((rc = stage_scan(idx, xq, B, K, nprobe, lb, ub_seed, ws, out_d, out_i, sp, st, mark))) return rc;
     TB_TRY(mark(TRIDENT_PHASES), "event");
     return TRIDENT_OK;
 }
@@ -303,6 +340,71 @@ int trident_search_profiled(const trident_index* idx, const float* xq, int32_t B
 }
 
 int64_t trident_launch_count(void) { return g_launches; }
+
+int trident_search_prep(const trident_index* idx, const float* xq, int32_t B, int32_t nprobe, void* workspace,
+                        size_t workspace_bytes, int32_t* probe_out, float* qrot_out, float* qinfo_out, void* stream) {
+    Workspace ws;
+    int rc = check_search_args(idx, xq, B, 1, nprobe, workspace, workspace_bytes, &ws);
+    if (rc) return rc;
+    if (B > 0 && (!probe_out || !qrot_out || !qinfo_out)) return fail(TRIDENT_ERR_INVALID, "an output is NULL");
+    if (B == 0) return TRIDENT_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
+    if ((rc = stage_coarse(idx, xq, B, nprobe, ws, nullptr, st))) return rc;
+    TB_TRY(cudaMemcpyAsync(probe_out, ws.probe, (size_t)B * nprobe * sizeof(int32_t), cudaMemcpyDeviceToDevice, st),
+           "probe copy");
+    TB_TRY(cudaMemcpyAsync(qrot_out, ws.qrot, (size_t)B * idx->D_pad * sizeof(float), cudaMemcpyDeviceToDevice, st),
+           "qrot copy");
+    TB_TRY(cudaMemcpyAsync(qinfo_out, ws.qinfo, (size_t)B * TRIDENT_QINFO_LEN * sizeof(float),
+                           cudaMemcpyDeviceToDevice, st),
+           "qinfo copy");
+    return TRIDENT_OK;
+}
+
+int trident_search_seed(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, int32_t mode,
+                        int32_t ub_seed, const int32_t* probe, const float* qrot, const float* qinfo, void* workspace,
+                        size_t workspace_bytes, float* seed_d, int64_t* seed_i, void* stream) {
+    Workspace ws;
+    int rc = check_search_args(idx, xq, B, K, nprobe, workspace, workspace_bytes, &ws);
+    if (rc) return rc;
+    if ((rc = resolve_mode(idx, B, nprobe, &mode, ub_seed))) return rc;
+    if (B > 0 && (!probe || !qrot || !qinfo || !seed_d || !seed_i))
+        return fail(TRIDENT_ERR_INVALID, "an input or seed output is NULL");
+    if (B == 0) return TRIDENT_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
+    TB_TRY(cudaMemcpyAsync(ws.probe, probe, (size_t)B * nprobe * sizeof(int32_t), cudaMemcpyDeviceToDevice, st),
+           "probe copy");
+    TB_TRY(cudaMemcpyAsync(ws.qrot, qrot, (size_t)B * idx->D_pad * sizeof(float), cudaMemcpyDeviceToDevice, st),
+           "qrot copy");
+    TB_TRY(cudaMemcpyAsync(ws.qinfo, qinfo, (size_t)B * TRIDENT_QINFO_LEN * sizeof(float), cudaMemcpyDeviceToDevice,
+                           st),
+           "qinfo copy");
+    TB_TRY(launch_fill_inf(ws.tau, B, st), "tau init");
+    const Marker nomark{nullptr, st};
+    if (mode != TRIDENT_MODE_CASCADE) {  // CM-FP32 has no seed: empty lists
+        TB_TRY(launch_fill_inf(reinterpret_cast<uint32_t*>(seed_d), B * K, st), "seed fill");
+        TB_TRY(cudaMemsetAsync(seed_i, 0xFF, (size_t)B * K * sizeof(int64_t), st), "seed fill");
+    }
+    return stage_seed(idx, xq, B, K, nprobe, mode == TRIDENT_MODE_CASCADE, ub_seed, ws, st, nomark, seed_d, seed_i);
+}
+
+int trident_search_finish(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
+                          int32_t mode, int32_t ub_seed, const float* tau_in, void* workspace, size_t workspace_bytes,
+                          float* out_d, int64_t* out_i, int64_t* stats, void* stream) {
+    Workspace ws;
+    int rc = check_search_args(idx, xq, B, K, nprobe, workspace, workspace_bytes, &ws);
+    if (rc) return rc;
+    if ((rc = resolve_mode(idx, B, nprobe, &mode, ub_seed))) return rc;
+    if (B > 0 && (!out_d || !out_i)) return fail(TRIDENT_ERR_INVALID, "out_d / out_i is NULL");
+    if (B == 0) return TRIDENT_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (tau_in)
+        TB_TRY(cudaMemcpyAsync(ws.tau, tau_in, (size_t)B * sizeof(float), cudaMemcpyDeviceToDevice, st), "tau copy");
+    const Marker nomark{nullptr, st};
+    return stage_scan(idx, xq, B, K, nprobe, mode == TRIDENT_MODE_CASCADE, ub_seed, ws, out_d, out_i,
+                      (unsigned long long*)stats, st, nomark);
+}
 
 int trident_merge_shards(const float* d_in, const int64_t* i_in, int32_t R, int32_t B, int32_t K, float* out_d,
                          int64_t* out_i, void* stream) {

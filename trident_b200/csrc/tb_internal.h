@@ -54,12 +54,17 @@ constexpr int kLptBins = 128;
 // into ws.items_lpt.
 cudaError_t launch_item_order(const trident_index& idx, int max_items, const Workspace& ws, cudaStream_t st);
 
+// tau[0..n) = +inf (float bits), tb_seed.cu.
+cudaError_t launch_fill_inf(uint32_t* tau, int n, cudaStream_t st);
+
 // Query-major threshold seeding (tb_seed.cu): rank the rows of each query's p_seed nearest lists by
 // a partial SQ8 distance, refine the best exactly (or bound them from above with ub) and store the
 // K-th value in ws.tau.
 int seed_lists_for(int B, int K, int nprobe);
+// seed_d/seed_i (optional, [B, K]) receive each query's K smallest seed values and their row ids;
+// shard = 1 sizes the refined set by the share of the seed lists this GPU holds.
 cudaError_t launch_seed(const trident_index& idx, const float* xq, const Workspace& ws, int B, int K, int nprobe,
-                        int p_seed, int ub, cudaStream_t st);
+                        int p_seed, int ub, float* seed_d, int64_t* seed_i, int shard, cudaStream_t st);
 
 // Scans and merges (tb_scan.cu).
 struct ScanLaunch {

@@ -15,13 +15,18 @@
 
 namespace tb {
 
+// A probe of an empty list (a list another GPU owns, in a sharded index) makes no pair.
+__device__ __forceinline__ bool probe_has_rows(int32_t c, int nlist, const int64_t* __restrict__ row_off) {
+    return (unsigned)c < (unsigned)nlist && row_off[c + 1] > row_off[c];
+}
+
 __global__ void pair_hist_kernel(const int32_t* __restrict__ probe, int64_t total, int nprobe, int p_init, int nlist,
-                                 int32_t* __restrict__ cnt) {
+                                 const int64_t* __restrict__ row_off, int32_t* __restrict__ cnt) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
         const int p = (int)(i % nprobe);
         const int s = p >= p_init;
         const int32_t c = probe[i];
-        if ((unsigned)c < (unsigned)nlist) atomicAdd(&cnt[s * nlist + c], 1);
+        if (probe_has_rows(c, nlist, row_off)) atomicAdd(&cnt[s * nlist + c], 1);
     }
 }
 
@@ -82,7 +87,8 @@ __global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t* __restri
 }
 
 __global__ void pair_scatter_kernel(const int32_t* __restrict__ probe, int64_t total, int nprobe, int p_init,
-                                    int nlist, int64_t base1, int32_t* __restrict__ cursor,
+                                    int nlist, const int64_t* __restrict__ row_off, int64_t base1,
+                                    int32_t* __restrict__ cursor,
                                     int32_t* __restrict__ pair_q, int32_t* __restrict__ pair_p, int K,
                                     float* __restrict__ cand_d, int32_t* __restrict__ cand_i) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
@@ -90,7 +96,7 @@ __global__ void pair_scatter_kernel(const int32_t* __restrict__ probe, int64_t t
         const int q = (int)(i / nprobe);
         const int s = p >= p_init;
         const int32_t c = probe[i];
-        if ((unsigned)c >= (unsigned)nlist) {  // no list for this probe: its slots stay empty
+        if (!probe_has_rows(c, nlist, row_off)) {  // no rows for this probe: its slots stay empty
             for (int k = 0; k < K; ++k) {
                 cand_d[i * K + k] = kInf;
                 cand_i[i * K + k] = -1;
@@ -133,9 +139,10 @@ cudaError_t launch_pairs(const trident_index& idx, const int32_t* probe, int B, 
     const int cap = num_sms() * 8;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    pair_hist_kernel<<<blocks, threads, 0, st>>>(probe, total, nprobe, p_init, nlist, ws.cnt);
+    pair_hist_kernel<<<blocks, threads, 0, st>>>(probe, total, nprobe, p_init, nlist, idx.list_row_off, ws.cnt);
     pair_scan_kernel<<<2, 1024, 0, st>>>(ws.cnt, nlist, G, ws.off, ws.item_off, ws.cursor, ws.ctr);
-    pair_scatter_kernel<<<blocks, threads, 0, st>>>(probe, total, nprobe, p_init, nlist, base1, ws.cursor, ws.pair_q,
+    pair_scatter_kernel<<<blocks, threads, 0, st>>>(probe, total, nprobe, p_init, nlist, idx.list_row_off, base1,
+                                                     ws.cursor, ws.pair_q,
                                                      ws.pair_p, K, ws.cand_d, ws.cand_i);
     dim3 g2((nlist + 255) / 256, 2);
     item_emit_kernel<<<g2, 256, 0, st>>>(ws.cnt, ws.off, ws.item_off, nlist, G, base1, ws.items);

@@ -37,8 +37,12 @@ struct SeedArgs {
     const float* qrot;
     const float* qinfo;
     const int32_t* probe;
+    const int32_t* oid;
     uint32_t* tau;
+    float* seed_d;    // optional [B, K]: the K smallest seed values per query, ascending (+inf padded)
+    int64_t* seed_i;  // optional [B, K]: their row ids (-1 padded)
     int D, D_pad, nb, T, nlist, nprobe, p_seed, K, S;
+    int shard;  // 1: the index holds only some lists; S shrinks with the share of local seed lists
     int ub;     // 1: SQ8 upper bounds of the selected rows instead of exact distances (no row reads)
     float rho;  // the index's relative slack of a float32 bound (lb_rel_slack)
 };
@@ -93,15 +97,18 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
     __shared__ int32_t s_len[kSeedListsMax];
     __shared__ int64_t s_r0[kSeedListsMax], s_t0[kSeedListsMax];
     __shared__ int s_w[kSeedThreads / 32];
-    __shared__ int s_n;
+    __shared__ int s_n, s_valid;
 
     const int q = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int T = a.T, nb = a.nb, D_pad = a.D_pad;
+    if (tid == 0) s_valid = 0;
+    __syncthreads();
     if (tid < kSeedListsMax) {  // the warm-up lists, loaded in parallel
         int c = -1, L = 0;
         if (tid < a.p_seed) {
             c = a.probe[(int64_t)q * a.nprobe + tid];
+            if ((unsigned)c < (unsigned)a.nlist) atomicAdd(&s_valid, 1);
             if ((unsigned)c < (unsigned)a.nlist) {
                 const int64_t r0 = a.row_off[c];
                 L = (int)(a.row_off[c + 1] - r0);
@@ -129,8 +136,21 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
     }
     __syncthreads();
     const int R = min(s_off[kSeedListsMax], kSeedRowsMax);
-    const int S = min(a.S, R);
-    if (S < a.K) return;  // fewer rows than K: no finite threshold from these lists
+    int S = a.S;
+    if (a.shard && s_valid > 0) {  // this GPU's share of the seed rows: in proportion to its lists
+        int m = 0;
+        while (m < kSeedListsMax && s_off[m] < s_off[m + 1]) ++m;
+        S = (a.S * m + s_valid - 1) / s_valid;
+    }
+    S = min(S, R);
+    if (a.seed_d) {
+        for (int k = tid; k < a.K; k += kSeedThreads) {  // slots beyond this GPU's rows stay empty
+            a.seed_d[(int64_t)q * a.K + k] = kInf;
+            a.seed_i[(int64_t)q * a.K + k] = -1;
+        }
+    }
+    if (S <= 0) return;
+    if (!a.shard && S < a.K) return;  // fewer rows than K: no finite threshold from these lists
 
     // ---- rank: squared distance of the SQ8 reconstruction over the leading blocks
     const int nbx = min(nb, kSeedBlocks);
@@ -228,6 +248,8 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
         int p = 0;
         while (i >= s_off[p + 1]) ++p;
         const int r = i - s_off[p];
+        __syncwarp();
+        if (lane == 0) s_sel[k] = a.oid[s_r0[p] + r];  // keep the row id for the seed list
         float d;
         if (a.ub) {
             const int64_t o = (int64_t)s_c[p] * D_pad;
@@ -258,11 +280,25 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
             const float e = s_dist[m];
             rank += (e < d) || (e == d && m < k);
         }
-        if (rank == a.K - 1) {
+        if (rank < a.K) {
             const float t = a.ub ? ub_threshold(d, a.qinfo[(int64_t)q * QI_LEN + QI_SIGMA], a.rho) : d;
-            atomicMin(a.tau + q, __float_as_uint(t));
+            if (rank == a.K - 1) atomicMin(a.tau + q, __float_as_uint(t));
+            if (a.seed_d) {
+                a.seed_d[(int64_t)q * a.K + rank] = t;
+                a.seed_i[(int64_t)q * a.K + rank] = s_sel[k];
+            }
         }
     }
+}
+
+__global__ void fill_inf_kernel(uint32_t* __restrict__ tau, int n) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) tau[i] = __float_as_uint(kInf);
+}
+
+cudaError_t launch_fill_inf(uint32_t* tau, int n, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    fill_inf_kernel<<<(n + 255) / 256 < 1024 ? (n + 255) / 256 : 1024, 256, 0, st>>>(tau, n);
+    return cudaGetLastError();
 }
 
 int seed_rows_for(int K) { return 32 * ((K + 31) / 32) < 64 ? 64 : 32 * ((K + 31) / 32); }
@@ -276,7 +312,7 @@ int seed_lists_for(int B, int K, int nprobe) {
 }
 
 cudaError_t launch_seed(const trident_index& idx, const float* xq, const Workspace& ws, int B, int K, int nprobe,
-                        int p_seed, int ub, cudaStream_t st) {
+                        int p_seed, int ub, float* seed_d, int64_t* seed_i, int shard, cudaStream_t st) {
     if (B <= 0 || p_seed <= 0) return cudaSuccess;
     SeedArgs a;
     a.xb = idx.xb_sorted;
@@ -290,7 +326,11 @@ cudaError_t launch_seed(const trident_index& idx, const float* xq, const Workspa
     a.qrot = ws.qrot;
     a.qinfo = ws.qinfo;
     a.probe = ws.probe;
+    a.oid = idx.orig_ids_sorted;
     a.tau = ws.tau;
+    a.seed_d = seed_d;
+    a.seed_i = seed_i;
+    a.shard = shard;
     a.D = idx.D;
     a.D_pad = idx.D_pad;
     a.nb = idx.num_blocks;

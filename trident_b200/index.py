@@ -345,6 +345,51 @@ class TridentV4Index:
             ms = ev0.elapsed_time(ev1)
         return topk_d, topk_i, ms
 
+    # ---- the search in three stages, for list sharding over GPUs (trident_b200.shard)
+    def search_prep(self, xq_gpu, nprobe: int):
+        """Stage 1 on this rank's own queries: (probe [B, nprobe] int32, qrot [B, D_pad] float32,
+        qinfo [B, 4] float32)."""
+        torch = _torch()
+        B = int(xq_gpu.shape[0])
+        ws = self._workspace(B, 1, nprobe)
+        probe = torch.empty((B, nprobe), dtype=torch.int32, device=self.dev)
+        qrot = torch.empty((B, self.D_pad), dtype=torch.float32, device=self.dev)
+        qinfo = torch.empty((B, _lib.QINFO_LEN), dtype=torch.float32, device=self.dev)
+        stream = torch.cuda.current_stream(self.dev)
+        _lib.check(_lib.lib().trident_search_prep(self.desc(), _ptr(xq_gpu), B, int(nprobe), _ptr(ws), ws.numel(),
+                                                  _ptr(probe), _ptr(qrot), _ptr(qinfo), stream.cuda_stream))
+        return probe, qrot, qinfo
+
+    def search_seed(self, xq_all, probe, qrot, qinfo, nprobe: int, k: int = 10, mode: int = 2, ub_seed: int = 0):
+        """Stage 2 on the gathered batch: work items over this rank's lists and each query's k
+        smallest seed values from this rank's rows. Returns (seed_d [B_all, k] float32, seed_i
+        [B_all, k] int64), ascending and padded with (+inf, -1); merged over the ranks, column k-1
+        is the threshold for search_finish. The workspace keeps the items for search_finish."""
+        torch = _torch()
+        B, K = int(xq_all.shape[0]), int(k)
+        ws = self._workspace(B, K, nprobe)
+        seed_d = torch.empty((B, K), dtype=torch.float32, device=self.dev)
+        seed_i = torch.empty((B, K), dtype=torch.int64, device=self.dev)
+        stream = torch.cuda.current_stream(self.dev)
+        _lib.check(_lib.lib().trident_search_seed(self.desc(), _ptr(xq_all), B, K, int(nprobe), int(mode),
+                                                  int(ub_seed), _ptr(probe), _ptr(qrot), _ptr(qinfo), _ptr(ws),
+                                                  ws.numel(), _ptr(seed_d), _ptr(seed_i), stream.cuda_stream))
+        return seed_d, seed_i
+
+    def search_finish(self, xq_all, tau, nprobe: int, k: int = 10, mode: int = 2, ub_seed: int = 0, stats_buf=None):
+        """Stage 3: the per-query top-k [B_all, k] of this rank's rows under the thresholds tau."""
+        torch = _torch()
+        B, K = int(xq_all.shape[0]), int(k)
+        ws = self._workspace(B, K, nprobe)
+        out_d = torch.empty((B, K), dtype=torch.float32, device=self.dev)
+        out_i = torch.empty((B, K), dtype=torch.int64, device=self.dev)
+        stream = torch.cuda.current_stream(self.dev)
+        sptr = _ptr(stats_buf) if stats_buf is not None else 0
+        _lib.check(_lib.lib().trident_search_finish(self.desc(), _ptr(xq_all), B, K, int(nprobe), int(mode),
+                                                    int(ub_seed), _ptr(tau), _ptr(ws), ws.numel(), _ptr(out_d),
+                                                    _ptr(out_i), sptr, stream.cuda_stream))
+        return out_d, out_i
+
     def coarse(self, xq_gpu, nprobe: int):
         """Exact probe lists (ascending by (float64 distance, list id)), their float64 distances and
         the float32 rotated queries."""

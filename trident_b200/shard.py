@@ -2,14 +2,21 @@
 
 The IVF lists are split across R ranks (greedy longest-first on list length, ties by list id).
 Every rank holds ALL centroids, mean64 and R64 but only the rows of its own lists: lists owned by
-other ranks are empty in its index. So every rank runs the identical coarse stage and selects the
-identical probe set with no communication, scans only its own lists, and produces a per-query
-top-K. The R lists are exchanged with one all-gather of [B, K] (float32 distance, int64 id) and
-merged by trident_merge_shards under the same (distance, id) order, which makes the sharded result
-identical to the single-GPU one.
+other ranks are empty in its index. Each rank brings its own B queries; a step over the R * B
+queries of all ranks runs the staged search:
 
-Optional threshold exchange (min-all-reduce of each query's K-th distance after the warm-up pass)
-is not needed for correctness; any rank's K-th distance bounds the global one.
+  1. coarse stage on the rank's own queries (probe lists, rotated queries, side info);
+  2. all-gather of those and of the query vectors over all ranks (NVLink);
+  3. pairs + Stage X seed of the whole batch over the local lists -> each query's K smallest
+     seed values of the local rows;
+  4. all-gather + merge of those lists -> each query's threshold: the K-th smallest over
+     distinct rows of all ranks, which bounds the final K-th distance;
+  5. Stage Y/Z over the local lists -> per-query top-K of the local rows [R * B, K];
+  6. all-to-all: rank r receives every rank's lists for its own B queries, and
+     trident_merge_shards merges them under the (distance, id) order.
+
+Per-rank work stays constant as R grows (1/R of the lists for R times the queries), so the
+bench reports weak scaling. The merged result is identical to the single-GPU one.
 """
 from typing import List
 
@@ -54,9 +61,10 @@ def merge_topk_host(d_all, i_all, K: int):
 class ShardedSearch:
     """Search over a list-sharded index with torch.distributed (NCCL on GPUs, gloo in tests).
 
-    `index` is this rank's TridentV4Index, built over the rows of its own lists (shard_rows) and the
-    full set of centroids. search() runs the local query path, all-gathers the [B, K] lists and
-    merges them on the device.
+    `index` is this rank's TridentV4Index, built over the rows of its own lists (shard_rows) and
+    the full set of centroids (any object with search_prep / search_seed / search_finish works).
+    search() takes this rank's own queries and returns their merged top-k. Every rank must call it
+    with the same batch size, k, nprobe and mode.
     """
 
     def __init__(self, index, group=None, merge=None):
@@ -68,21 +76,62 @@ class ShardedSearch:
         self.rank = dist.get_rank(group)
         self.merge = merge  # (d_all [R,B,K], i_all [R,B,K]) -> (d, i); None: the device merge
 
-    def search(self, xq_gpu, nprobe: int, k: int = 10, mode: int = 2, ub_seed: int = 0, phase_ms=None):
-        import torch
-        import torch.distributed as dist
-
-        d_loc, i_loc, _ = self.index.search(xq_gpu, nprobe, mode=mode, k=k, ub_seed=ub_seed, phase_ms=phase_ms)
-        B = d_loc.shape[0]
-        # rank-major [R * B, K] (the shape every backend accepts), viewed as [R, B, K]
-        d_all = torch.empty((self.world * B, k), dtype=torch.float32, device=d_loc.device)
-        i_all = torch.empty((self.world * B, k), dtype=torch.int64, device=d_loc.device)
-        dist.all_gather_into_tensor(d_all, d_loc.contiguous(), group=self.group)
-        dist.all_gather_into_tensor(i_all, i_loc.contiguous(), group=self.group)
-        d_all = d_all.view(self.world, B, k)
-        i_all = i_all.view(self.world, B, k)
+    def _merge(self, d_all, i_all):
         if self.merge is not None:
             return self.merge(d_all, i_all)
         from .index import merge_shards
 
         return merge_shards(d_all, i_all)
+
+    def _gather(self, t):
+        import torch
+        import torch.distributed as dist
+
+        out = torch.empty((self.world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
+        return out
+
+    def search(self, xq, nprobe: int, k: int = 10, mode: int = 2, ub_seed: int = 0, phase_ms=None):
+        import torch
+        import torch.distributed as dist
+
+        R, B = self.world, int(xq.shape[0])
+        timed = phase_ms is not None and xq.is_cuda
+        evs = []
+
+        def mark(name):
+            if timed:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                evs.append((name, e))
+
+        mark("coarse")
+        probe, qrot, qinfo = self.index.search_prep(xq, nprobe)
+        mark("gather")
+        xq_all, probe_all = self._gather(xq), self._gather(probe)
+        qrot_all, qinfo_all = self._gather(qrot), self._gather(qinfo)
+        mark("seed")
+        seed_d, seed_i = self.index.search_seed(xq_all, probe_all, qrot_all, qinfo_all, nprobe, k=k, mode=mode,
+                                                ub_seed=ub_seed)
+        mark("tau")
+        sd_all = self._gather(seed_d).view(R, R * B, k)
+        si_all = self._gather(seed_i).view(R, R * B, k)
+        tau = self._merge(sd_all, si_all)[0][:, k - 1].contiguous()
+        mark("scan")
+        d_loc, i_loc = self.index.search_finish(xq_all, tau, nprobe, k=k, mode=mode, ub_seed=ub_seed)
+        mark("exchange")
+        # rank-major chunks of B queries: rank r receives chunk r of every rank -> [R, B, k]
+        d_in = torch.empty_like(d_loc)
+        i_in = torch.empty_like(i_loc)
+        dist.all_to_all_single(d_in, d_loc.contiguous(), group=self.group)
+        dist.all_to_all_single(i_in, i_loc.contiguous(), group=self.group)
+        d_in, i_in = d_in.view(R, B, k), i_in.view(R, B, k)
+        mark("merge")
+        out = self._merge(d_in, i_in)
+        mark("end")
+        if timed:
+            evs[-1][1].synchronize()
+            phase_ms.clear()
+            for (n, a), (_, b) in zip(evs[:-1], evs[1:]):
+                phase_ms[n] = a.elapsed_time(b)
+        return out
