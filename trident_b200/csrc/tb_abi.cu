@@ -216,11 +216,40 @@ struct Marker {
     }
 };
 
+// A second stream (and its fork/join events) per calling thread and device: the tensor-core GEMM
+// runs beside the float64 rotation, which it does not depend on. Both fit on one SM together.
+struct SideStream {
+    cudaStream_t s = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+
+static cudaError_t side_stream(SideStream** out) {
+    static thread_local SideStream per_dev[64];
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 0 || dev >= 64) dev = 0;
+    SideStream& ss = per_dev[dev];
+    if (!ss.s) {
+        if ((e = cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking)) != cudaSuccess) return e;
+        if ((e = cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming)) != cudaSuccess) return e;
+        if ((e = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming)) != cudaSuccess) return e;
+    }
+    *out = &ss;
+    return cudaSuccess;
+}
+
 // Stage 1 of a search: rotation, coarse GEMM and exact probe selection for B queries, into ws.
 static int stage_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t nprobe, const Workspace& ws,
                         unsigned long long* sp, cudaStream_t st) {
+    SideStream* ss = nullptr;
+    TB_TRY(side_stream(&ss), "side stream");
+    TB_TRY(cudaEventRecord(ss->fork, st), "fork");
+    TB_TRY(cudaStreamWaitEvent(ss->s, ss->fork, 0), "fork");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, ss->s), "coarse_gemm");
+    TB_TRY(cudaEventRecord(ss->join, ss->s), "join");
     TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, st), "coarse_gemm");
+    TB_TRY(cudaStreamWaitEvent(st, ss->join, 0), "join");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
     g_launches += 4;
     return TRIDENT_OK;

@@ -52,22 +52,26 @@ constexpr int kMaxG = 64;
 constexpr int kScanThreadsPerSm = 512;
 
 // Stage Y on one 32-dim block: acc += sum_d max(|code_d delta_d + (vmin_d - q~_d)| - eps_d, 0)^2
-// (reference :750-767). base/dl/ep point at the block's 32 entries in shared memory.
+// (reference :750-767). base/dl/ep point at the block's 32 entries in shared memory. Pairs of dims
+// go through packed FFMA2 (each lane of the pair rounds like fmaf); the sum runs as two chains,
+// which the float32 slack of the prune test covers like any other order.
 __device__ __forceinline__ float lb_block(const uint4 w0, const uint4 w1, const float* __restrict__ base,
                                           const float* __restrict__ dl, const float* __restrict__ ep, float acc) {
     const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float2 a2 = make_float2(acc, 0.0f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float4 b4 = *reinterpret_cast<const float4*>(base + 4 * i);
         const float4 d4 = *reinterpret_cast<const float4*>(dl + 4 * i);
         const float4 e4 = *reinterpret_cast<const float4*>(ep + 4 * i);
-        float l;
-        l = fmaxf(fabsf(fmaf(u8f(w[i], 0), d4.x, b4.x)) - e4.x, 0.0f); acc = fmaf(l, l, acc);
-        l = fmaxf(fabsf(fmaf(u8f(w[i], 1), d4.y, b4.y)) - e4.y, 0.0f); acc = fmaf(l, l, acc);
-        l = fmaxf(fabsf(fmaf(u8f(w[i], 2), d4.z, b4.z)) - e4.z, 0.0f); acc = fmaf(l, l, acc);
-        l = fmaxf(fabsf(fmaf(u8f(w[i], 3), d4.w, b4.w)) - e4.w, 0.0f); acc = fmaf(l, l, acc);
+        const float2 u01 = __ffma2_rn(u8f2(w[i], 0), make_float2(d4.x, d4.y), make_float2(b4.x, b4.y));
+        const float2 u23 = __ffma2_rn(u8f2(w[i], 2), make_float2(d4.z, d4.w), make_float2(b4.z, b4.w));
+        const float2 l01 = make_float2(fmaxf(fabsf(u01.x) - e4.x, 0.0f), fmaxf(fabsf(u01.y) - e4.y, 0.0f));
+        const float2 l23 = make_float2(fmaxf(fabsf(u23.x) - e4.z, 0.0f), fmaxf(fabsf(u23.y) - e4.w, 0.0f));
+        a2 = __ffma2_rn(l01, l01, a2);
+        a2 = __ffma2_rn(l23, l23, a2);
     }
-    return acc;
+    return a2.x + a2.y;
 }
 
 // SQ8 upper bound on one block: acc += sum_d (|code_d delta_d + (vmin_d - q~_d)| + eps_d)^2
