@@ -216,8 +216,9 @@ struct Marker {
     }
 };
 
-// A second stream (and its fork/join events) per calling thread and device: the tensor-core GEMM
-// runs beside the float64 rotation, which it does not depend on. Both fit on one SM together.
+// A second stream (and its fork/join events) per calling thread and device. The float64 rotation
+// runs there: the coarse GEMM, the probe selection and the pair lists need only the queries and
+// their norms, so the rotation overlaps all of them and is joined before the seed kernel.
 struct SideStream {
     cudaStream_t s = nullptr;
     cudaEvent_t fork = nullptr, join = nullptr;
@@ -244,14 +245,22 @@ static int stage_coarse(const trident_index* idx, const float* xq, int32_t B, in
                         unsigned long long* sp, cudaStream_t st) {
     SideStream* ss = nullptr;
     TB_TRY(side_stream(&ss), "side stream");
+    TB_TRY(launch_query_norms(*idx, xq, B, ws.qinfo, ws.tau, st), "query norms");
     TB_TRY(cudaEventRecord(ss->fork, st), "fork");
     TB_TRY(cudaStreamWaitEvent(ss->s, ss->fork, 0), "fork");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, ss->s), "coarse_gemm");
+    TB_TRY(launch_rotate_f64(*idx, xq, B, ws.qrot, ss->s), "rotate");
     TB_TRY(cudaEventRecord(ss->join, ss->s), "join");
-    TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
-    TB_TRY(cudaStreamWaitEvent(st, ss->join, 0), "join");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, st), "coarse_gemm");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
     g_launches += 4;
+    return TRIDENT_OK;
+}
+
+// The caller's stream waits for the rotation that stage_coarse started on the side stream.
+static int join_rotation(cudaStream_t st) {
+    SideStream* ss = nullptr;
+    TB_TRY(side_stream(&ss), "side stream");
+    TB_TRY(cudaStreamWaitEvent(st, ss->join, 0), "join");
     return TRIDENT_OK;
 }
 
@@ -261,11 +270,13 @@ static int stage_coarse(const trident_index* idx, const float* xq, int32_t B, in
 static int stage_seed(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, bool lb,
                       int32_t ub_seed, const Workspace& ws, cudaStream_t st, const Marker& mark,
                       float* seed_d = nullptr, int64_t* seed_i = nullptr) {
+    int rc_join = 0;
     const int G = scan_group_size(*idx, K);
     TB_TRY(mark(TRIDENT_PHASE_PAIRS), "event");
     TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, 0, G, K, ws, st), "pairs");
     TB_TRY(launch_item_order(*idx, B * nprobe, ws, st), "item order");
     g_launches += 7;
+    if ((rc_join = join_rotation(st))) return rc_join;  // qrot is read from here on
     if (lb) {
         TB_TRY(mark(TRIDENT_PHASE_SEED), "event");
         TB_TRY(launch_seed(*idx, xq, ws, B, K, nprobe, seed_lists_for(B, K, nprobe), ub_seed >= 1, seed_d, seed_i,
@@ -320,7 +331,7 @@ static int search_impl(const trident_index* idx, const float* xq, int32_t B, int
     TB_TRY(mark(TRIDENT_PHASE_COARSE), "event");
     TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
     if ((rc = stage_coarse(idx, xq, B, nprobe, ws, sp, st))) return rc;
-    if ((rc = stage_seed(idx, xq, B, K, nprobe, lb, ub_seed, ws, st, mark))) return rc;
+    if ((rc = stage_seed(idx, xq, B, K, nprobe, lb, ub_seed, ws, st, mark))) return rc;  // joins the rotation
     if ((rc = stage_scan(idx, xq, B, K, nprobe, lb, ub_seed, ws, out_d, out_i, sp, st, mark))) return rc;
     TB_TRY(mark(TRIDENT_PHASES), "event");
     return TRIDENT_OK;
@@ -380,6 +391,7 @@ int trident_search_prep(const trident_index* idx, const float* xq, int32_t B, in
     cudaStream_t st = (cudaStream_t)stream;
     TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
     if ((rc = stage_coarse(idx, xq, B, nprobe, ws, nullptr, st))) return rc;
+    if ((rc = join_rotation(st))) return rc;
     TB_TRY(cudaMemcpyAsync(probe_out, ws.probe, (size_t)B * nprobe * sizeof(int32_t), cudaMemcpyDeviceToDevice, st),
            "probe copy");
     TB_TRY(cudaMemcpyAsync(qrot_out, ws.qrot, (size_t)B * idx->D_pad * sizeof(float), cudaMemcpyDeviceToDevice, st),

@@ -158,12 +158,23 @@ __global__ void __launch_bounds__(256) query_norms_kernel(const float* __restric
     }
 }
 
-cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
-                          uint32_t* tau, cudaStream_t st) {
+cudaError_t launch_query_norms(const trident_index& idx, const float* xq, int B, float* qinfo, uint32_t* tau,
+                               cudaStream_t st) {
     query_norms_kernel<<<(B + 7) / 8, 256, 0, st>>>(xq, idx.pca_mean, B, idx.D, idx.D_pad, qinfo, tau);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_rotate_f64(const trident_index& idx, const float* xq, int B, float* qrot, cudaStream_t st) {
     dim3 grid((B + kRM - 1) / kRM, (idx.D_pad + kRN - 1) / kRN);
     rotate_f64_kernel<<<grid, 256, 0, st>>>(xq, idx.pca_mean, idx.pca_rot, B, idx.D, idx.D_pad, qrot);
     return cudaGetLastError();
+}
+
+cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
+                          uint32_t* tau, cudaStream_t st) {
+    cudaError_t e = launch_query_norms(idx, xq, B, qinfo, tau, st);
+    if (e != cudaSuccess) return e;
+    return launch_rotate_f64(idx, xq, B, qrot, st);
 }
 
 // ------------------------------------------------------------------------------------------

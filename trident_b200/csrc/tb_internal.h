@@ -37,6 +37,11 @@ struct Workspace {
 size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void* base, Workspace* ws);
 
 // Coarse stage (tb_coarse.cu).
+// Per-query norms and sigma into qinfo, tau = +inf (query_norms_kernel), and the float64 rotation
+// into qrot (rotate_f64_kernel); launch_rotate runs both on one stream.
+cudaError_t launch_query_norms(const trident_index& idx, const float* xq, int B, float* qinfo, uint32_t* tau,
+                               cudaStream_t st);
+cudaError_t launch_rotate_f64(const trident_index& idx, const float* xq, int B, float* qrot, cudaStream_t st);
 cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
                           uint32_t* tau, cudaStream_t st);
 // tcgen05 3xTF32 GEMM (tb_coarse_mma.cu); sets *err = 2 if a bounded wait gave up.

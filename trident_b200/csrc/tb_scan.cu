@@ -132,23 +132,27 @@ __device__ __forceinline__ float bound_block_g(const uint4 w0, const uint4 w1, c
                                                const float* __restrict__ qr, const float* __restrict__ dl,
                                                const float* __restrict__ ep, float acc) {
     const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+    float2 a2 = make_float2(acc, 0.0f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const float4 v4 = __ldg(reinterpret_cast<const float4*>(vm) + i);
         const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr) + i);
         const float4 d4 = *reinterpret_cast<const float4*>(dl + 4 * i);
         const float4 e4 = *reinterpret_cast<const float4*>(ep + 4 * i);
-        const float b[4] = {v4.x - q4.x, v4.y - q4.y, v4.z - q4.z, v4.w - q4.w};
-        const float dd[4] = {d4.x, d4.y, d4.z, d4.w};
-        const float ee[4] = {e4.x, e4.y, e4.z, e4.w};
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float u = fabsf(fmaf(u8f(w[i], k), dd[k], b[k]));
-            const float l = UPPER ? u + ee[k] : fmaxf(u - ee[k], 0.0f);
-            acc = fmaf(l, l, acc);
+        const float2 u01 = __ffma2_rn(u8f2(w[i], 0), make_float2(d4.x, d4.y), make_float2(v4.x - q4.x, v4.y - q4.y));
+        const float2 u23 = __ffma2_rn(u8f2(w[i], 2), make_float2(d4.z, d4.w), make_float2(v4.z - q4.z, v4.w - q4.w));
+        float2 l01, l23;
+        if (UPPER) {
+            l01 = make_float2(fabsf(u01.x) + e4.x, fabsf(u01.y) + e4.y);
+            l23 = make_float2(fabsf(u23.x) + e4.z, fabsf(u23.y) + e4.w);
+        } else {
+            l01 = make_float2(fmaxf(fabsf(u01.x) - e4.x, 0.0f), fmaxf(fabsf(u01.y) - e4.y, 0.0f));
+            l23 = make_float2(fmaxf(fabsf(u23.x) - e4.z, 0.0f), fmaxf(fabsf(u23.y) - e4.w, 0.0f));
         }
+        a2 = __ffma2_rn(l01, l01, a2);
+        a2 = __ffma2_rn(l23, l23, a2);
     }
-    return acc;
+    return a2.x + a2.y;
 }
 
 constexpr float kU32 = 5.9604644775390625e-08f;  // 2^-24
