@@ -24,39 +24,49 @@
 namespace tb {
 
 // ------------------------------------------------------------------------------------------
-// Rotation: qrot[j][d] = float((q_j - mu) R[:, d]) with k ascending and fma (the oracle's
-// oracle_rotate_f64), as a register-tiled float64 GEMM: 64 queries x 128 dims per CTA, 16-deep
-// k-slices, 4 x 8 outputs per thread. The next k-slice is loaded into registers while the current
-// one is multiplied from shared memory (two buffers), so global latency overlaps the DFMAs. The
-// k order of every output stays sequential, so the result is bit-identical to the oracle.
+// Rotation: qrot[j][d] = float((q_j - mu) R[:, d]) in float64 on the FP64 tensor cores
+// (mma.sync m8n8k4 f64, DMMA). A CTA computes 64 queries x 128 dims with 8 warps of 32 x 32
+// (4 x 4 tiles of 8 x 8); 8-deep k-slices are staged in shared memory in two buffers, the next
+// slice loaded into registers while the current one is multiplied. The products accumulate in
+// float64 in k order in steps of 4; the error bound folded into sigma, (D + 2) 2^-52 relative to
+// sum_k |q_k - mu_k| |R_kd|, holds for any rounding inside a step. The result is rounded once to
+// float32.
 // ------------------------------------------------------------------------------------------
-constexpr int kRM = 64, kRN = 128, kRK = 16;
+constexpr int kRM = 64, kRN = 128, kRK = 8;
+constexpr int kRAP = kRK + 4;   // padded row of the query slice (conflict-free fragment reads)
+constexpr int kRBP = kRN + 8;   // padded row of the R slice
+
+__device__ __forceinline__ void dmma_8x8x4(double& d0, double& d1, double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+                 : "+d"(d0), "+d"(d1)
+                 : "d"(a), "d"(b));
+}
 
 __global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict__ xq, const double* __restrict__ mu,
                                                         const double* __restrict__ R, int B, int D, int D_pad,
                                                         float* __restrict__ qrot) {
-    __shared__ __align__(16) double sQ[2][kRK][kRM];
-    __shared__ __align__(16) double sR[2][kRK][kRN];
-    const int tid = threadIdx.x;
-    const int tx = tid & 15, ty = tid >> 4;  // rows ty*4..+3, columns tx + 16*j
+    __shared__ __align__(16) double sA[2][kRM][kRAP];
+    __shared__ __align__(16) double sB[2][kRK][kRBP];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int wm = (warp & 1) * 32, wn = (warp >> 1) * 32;  // the warp's 32 x 32 tile
     const int m0 = blockIdx.x * kRM, n0 = blockIdx.y * kRN;
-    double acc[4][8];
+    double acc[4][4][2];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
-    // staging assignment: 4 (row, k) elements of the query slice and 8 (k, column) of R per thread
-    double rq[4], rr[8];
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+    constexpr int kQA = kRM * kRK / 256, kQB = kRK * kRN / 256;  // staged values per thread
+    double rq[kQA], rr[kQB];
     auto fetch = [&](int k0) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kQA; ++t) {
             const int i = tid + 256 * t;
             const int r = i / kRK, k = i - r * kRK;
             const int gm = m0 + r, gk = k0 + k;
             rq[t] = (gm < B && gk < D) ? (double)__ldg(xq + (int64_t)gm * D + gk) - __ldg(mu + gk) : 0.0;
         }
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
+        for (int t = 0; t < kQB; ++t) {
             const int i = tid + 256 * t;
             const int k = i / kRN, n = i - k * kRN;
             const int gk = k0 + k, gn = n0 + n;
@@ -65,43 +75,39 @@ __global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict
     };
     auto stash = [&](int buf) {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
+        for (int t = 0; t < kQA; ++t) {
             const int i = tid + 256 * t;
             const int r = i / kRK, k = i - r * kRK;
-            sQ[buf][k][r] = rq[t];
+            sA[buf][r][k] = rq[t];
         }
 #pragma unroll
-        for (int t = 0; t < 8; ++t) {
+        for (int t = 0; t < kQB; ++t) {
             const int i = tid + 256 * t;
             const int k = i / kRN, n = i - k * kRN;
-            sR[buf][k][n] = rr[t];
+            sB[buf][k][n] = rr[t];
         }
     };
-    auto step = [&](int buf, int k) {
-        const double2 a01 = *reinterpret_cast<const double2*>(&sQ[buf][k][ty * 4]);
-        const double2 a23 = *reinterpret_cast<const double2*>(&sQ[buf][k][ty * 4 + 2]);
-        const double a[4] = {a01.x, a01.y, a23.x, a23.y};
-        double b[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) b[j] = sR[buf][k][tx + 16 * j];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[i][j] = fma(a[i], b[j], acc[i][j]);
-    };
+    // fragments of m8n8k4 (row.col): A[row = lane/4][k = lane%4], B[k = lane%4][col = lane/4],
+    // D rows lane/4, columns 2 (lane%4) + {0, 1}
+    const int fr = lane >> 2, fk = lane & 3;
     fetch(0);
     stash(0);
     __syncthreads();
     int buf = 0;
     for (int k0 = 0; k0 < D; k0 += kRK) {
         const bool more = k0 + kRK < D;
-        if (more) fetch(k0 + kRK);  // in flight during this slice's DFMAs
-        const int kn = min(kRK, D - k0);
-        if (kn == kRK) {
+        if (more) fetch(k0 + kRK);  // in flight during this slice's DMMAs
 #pragma unroll
-            for (int k = 0; k < kRK; ++k) step(buf, k);
-        } else {
-            for (int k = 0; k < kn; ++k) step(buf, k);
+        for (int ks = 0; ks < kRK; ks += 4) {
+            double a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = sA[buf][wm + 8 * i + fr][ks + fk];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = sB[buf][ks + fk][wn + 8 * j + fr];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_8x8x4(acc[i][j][0], acc[i][j][1], a[i], b[j]);
         }
         if (more) {
             stash(buf ^ 1);
@@ -111,13 +117,15 @@ __global__ void __launch_bounds__(256) rotate_f64_kernel(const float* __restrict
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const int gm = m0 + ty * 4 + i;
+        const int gm = m0 + wm + 8 * i + fr;
         if (gm >= B) continue;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int gn = n0 + tx + 16 * j;
-            if (gn < D_pad) qrot[(int64_t)gm * D_pad + gn] = gn < D ? (float)acc[i][j] : 0.0f;
-        }
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int gn = n0 + wn + 8 * j + 2 * fk + h;
+                if (gn < D_pad) qrot[(int64_t)gm * D_pad + gn] = gn < D ? (float)acc[i][j][h] : 0.0f;
+            }
     }
 }
 
