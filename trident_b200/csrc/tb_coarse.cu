@@ -188,7 +188,7 @@ cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, floa
 // ------------------------------------------------------------------------------------------
 // Exact top-nprobe selection, one CTA per query.
 // ------------------------------------------------------------------------------------------
-constexpr int kSelThreads = 512;
+constexpr int kSelThreads = 256;
 constexpr int kSelNW = kSelThreads / 32;
 constexpr int kSelCap = 2048;        // sorted best (<= nprobe <= 1024) + one batch of re-check members
 constexpr int kSelSmemKeys = 8192;   // approximate distances cached in shared memory up to this nlist
@@ -254,7 +254,7 @@ __device__ __forceinline__ double l2_f64_warp(const float* __restrict__ qv, cons
     return total;
 }
 
-__global__ void __launch_bounds__(kSelThreads) probe_select_kernel(
+__global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
     const float* __restrict__ coarse, const float* __restrict__ xq, const float* __restrict__ cent,
     const float* __restrict__ qinfo, int nlist, int D, int nprobe, float cmax, int32_t* __restrict__ probe,
     double* __restrict__ probe_d64, unsigned long long* __restrict__ stats) {

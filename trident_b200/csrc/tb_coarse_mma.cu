@@ -42,7 +42,7 @@ constexpr int kCStageBytes = 2 * kCAbytes + 2 * kCBbytes;
 // way round would still address only this CTA's shared memory
 constexpr int kCSmem = 2 * kCStageBytes + 32768 + 1024;
 constexpr uint32_t kCWaitTries = 1u << 22;       // bounded mbarrier polling
-constexpr uint32_t kCTmemCols = 128;
+constexpr uint32_t kCTmemCols = kCN;  // one float32 column per list of the tile (a power of 2 >= 32)
 
 // Instruction descriptor: D = F32 (bits 4-5 = 1), A = B = TF32 (bits 7-9, 10-12 = 2), both
 // K-major, N >> 3 at bits 17-22, M >> 4 at bits 24-28.
@@ -121,14 +121,16 @@ __device__ __forceinline__ void load_split_row(const float* __restrict__ src, in
     }
 }
 
+// rows = the tile's row count (the chunk stride of the chunk-major layout)
+template <int ROWS>
 __device__ __forceinline__ void store_split(unsigned char* hi, unsigned char* lo, int r, const float4 (&v)[kCChunks]) {
 #pragma unroll
     for (int c = 0; c < kCChunks; ++c) {
         const float4 x = v[c];
         const float4 h = make_float4(tf32_hi(x.x), tf32_hi(x.y), tf32_hi(x.z), tf32_hi(x.w));
         const float4 l = make_float4(tf32_hi(x.x - h.x), tf32_hi(x.y - h.y), tf32_hi(x.z - h.z), tf32_hi(x.w - h.w));
-        *reinterpret_cast<float4*>(hi + ((size_t)c * kCM + r) * 16) = h;
-        *reinterpret_cast<float4*>(lo + ((size_t)c * kCM + r) * 16) = l;
+        *reinterpret_cast<float4*>(hi + ((size_t)c * ROWS + r) * 16) = h;
+        *reinterpret_cast<float4*>(lo + ((size_t)c * ROWS + r) * 16) = l;
     }
 }
 
@@ -172,14 +174,14 @@ __global__ void __launch_bounds__(kCThreads, 1) coarse_mma_kernel(const float* _
         unsigned char* bL = bH + kCBbytes;
         float4 va[kCChunks], vb[kCChunks];
         load_split_row<VEC>(xq, B, D, m0 + tid, kt * kCK, va);
-        load_split_row<VEC>(cent, nlist, D, n0 + tid, kt * kCK, vb);
+        if (tid < kCN) load_split_row<VEC>(cent, nlist, D, n0 + tid, kt * kCK, vb);
         if (kt >= 2 && !mbar_wait(&s_bar[s], (uint32_t)((kt - 2) >> 1) & 1u)) ok = false;  // stage free?
         if (!__syncthreads_and(ok)) {
             ok = false;
             break;
         }
-        store_split(aH, aL, tid, va);
-        store_split(bH, bL, tid, vb);
+        store_split<kCM>(aH, aL, tid, va);
+        if (tid < kCN) store_split<kCN>(bH, bL, tid, vb);
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> tensor core
         __syncthreads();
         if (tid == 0) {
