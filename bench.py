@@ -51,13 +51,18 @@ def parse_args():
     p.add_argument("--nprobe", type=int, default=0)
     p.add_argument("--k", type=int, default=0)
     p.add_argument("--mode", type=int, default=-1, help="-1 router, 2 cascade, 10 CM-FP32")
-    p.add_argument("--ub-seed", type=int, default=0)
+    p.add_argument("--ub-seed", type=int, default=-1, help="0/1/2 (default: 0, or 1 with --ooc)")
+    p.add_argument("--ooc", action="store_true",
+                   help="zero-copy out-of-core: FP32 rows in pinned host memory, read over PCIe by Stage Z")
     p.add_argument("--check", type=int, default=64, help="queries verified against the CPU oracle")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU seconds of the CPU baseline")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-roofline", action="store_true")
     p.add_argument("--n", type=int, default=0, help="override N (rows) for quick runs")
-    return p.parse_args()
+    a = p.parse_args()
+    if a.ub_seed < 0:  # out of core, seed from SQ8 upper bounds: the seed then reads no FP32 row
+        a.ub_seed = 1 if a.ooc else 0
+    return a
 
 
 # ----------------------------------------------------------------------------------------------
@@ -220,10 +225,10 @@ def make_workload(args, d: Dist):
         counts = np.bincount(l_np, minlength=cfg.nlist)
         owner = torch.from_numpy(partition_lists(counts, d.world)).to(d.dev)
         rows = torch.nonzero(owner[lids.long()] == d.rank).flatten()
-        st = SharedClusterStorage(xb[rows], lids[rows], None, cfg.nlist, device=d.dev)
+        st = SharedClusterStorage(xb[rows], lids[rows], None, cfg.nlist, device=d.dev, host_rows=args.ooc)
         st.orig_ids_sorted = rows.to(torch.int32)[st.orig_ids_sorted.long()].contiguous()
     else:
-        st = SharedClusterStorage(xb, lids, None, cfg.nlist, device=d.dev)
+        st = SharedClusterStorage(xb, lids, None, cfg.nlist, device=d.dev, host_rows=args.ooc)
     idx = TridentV4Index(st, c_np, mu_np, R_np, tile_size=choose_tile(cfg.D), device=d.dev, max_batch=cfg.B,
                          max_nprobe=cfg.nprobe, max_k=cfg.K)
     torch.cuda.synchronize()
@@ -332,6 +337,26 @@ def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks):
         "pairs": int(p1.size), "candidates": int(cand.sum()), "blocks": int(blocks.sum()),
         "survivor_pairs": int(surv.sum()), "survivor_rows": surv_rows, "profile_s": round(prof_s, 2),
     }
+
+
+def pcie_accounting(idx, cfg, xq_dev, nprobe, K, mode, ub_seed, ms_per_step):
+    """Out-of-core PCIe traffic of one step. Every Stage-Z refine reads one FP32 row (D x 4 bytes) from
+    pinned host memory through UVA. The seed then reads no row (ub_seed >= 1: SQ8 upper bounds), so
+    the rows crossing PCIe are the scan's survivors (statistics slot TRIDENT_STAT_SURVIVORS). With
+    ub_seed = 0 the seed's refined rows come on top. They are bounded here by B x seed rows."""
+    import torch
+
+    st = torch.zeros(8, dtype=torch.int64, device=xq_dev.device)
+    idx.search(xq_dev, nprobe, mode=mode, k=K, ub_seed=ub_seed, stats_buf=st)
+    torch.cuda.synchronize()
+    surv = int(st[2].item())
+    row = cfg.D * 4
+    seed_rows = 0 if ub_seed >= 1 or mode != 2 else cfg.B * max(64, 32 * ((K + 31) // 32))
+    by = (surv + seed_rows) * row
+    gbs = by / (ms_per_step * 1e-3) / 1e9
+    return {"rows_in": "pinned host memory (zero-copy, read through UVA)", "survivor_rows": surv,
+            "seed_rows_bound": seed_rows, "pcie_bytes_per_step": by, "pcie_gbs": round(gbs, 2),
+            "pcie_nominal_gbs": 64.0, "pcie_frac_of_nominal": round(gbs / 64.0, 4)}
 
 
 def traffic_from_profile():
@@ -457,6 +482,9 @@ def run_ours(args, d: Dist):
         cpu = None
         if not args.no_cpu_baseline and d.world == 1:
             cpu = cpu_baseline(args, cfg, xq, c_np, xs, perm, off)
+        ooc = None
+        if args.ooc and d.world == 1:
+            ooc = pcie_accounting(idx, cfg, xq_dev, nprobe, K, mode, args.ub_seed, ms_per_step)
         result = {
             "metric": METRIC, "value": round(B * d.world / (ms_per_step * 1e-3), 1), "unit": UNIT,
             "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
@@ -479,6 +507,7 @@ def run_ours(args, d: Dist):
                     "d2h_bytes_per_step": int(out_d_h.numel() * 4 + out_i_h.numel() * 8) * d.world},
             "gpu_launches": launches, "clocks": clk, "lossless_check": check,
             "roofline": roof, "cpu_baseline": cpu,
+            **({"ooc": ooc} if ooc is not None else {}),
         }
     return result
 

@@ -230,7 +230,11 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
         }
     }
     __syncthreads();
-    if (s_n < S) {
+    // Every thread reads the count before any thread adds to it again: a thread that read it late
+    // would skip the branch and its barrier while the others wait inside.
+    const int n_below = s_n;
+    __syncthreads();
+    if (n_below < S) {
         for (int i = tid; i < R; i += kSeedThreads) {
             if (s_key[i] == v) {
                 const int k = atomicAdd(&s_n, 1);
