@@ -221,7 +221,8 @@ struct Marker {
 // their norms, so the rotation overlaps all of them and is joined before the seed kernel.
 struct SideStream {
     cudaStream_t s = nullptr;
-    cudaEvent_t fork = nullptr, join = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;    // around the rotation
+    cudaEvent_t fork2 = nullptr, join2 = nullptr;  // around the pair lists and work items
 };
 
 static cudaError_t side_stream(SideStream** out) {
@@ -235,6 +236,8 @@ static cudaError_t side_stream(SideStream** out) {
         if ((e = cudaStreamCreateWithFlags(&ss.s, cudaStreamNonBlocking)) != cudaSuccess) return e;
         if ((e = cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming)) != cudaSuccess) return e;
         if ((e = cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming)) != cudaSuccess) return e;
+        if ((e = cudaEventCreateWithFlags(&ss.fork2, cudaEventDisableTiming)) != cudaSuccess) return e;
+        if ((e = cudaEventCreateWithFlags(&ss.join2, cudaEventDisableTiming)) != cudaSuccess) return e;
     }
     *out = &ss;
     return cudaSuccess;
@@ -270,11 +273,18 @@ static int join_rotation(cudaStream_t st) {
 static int stage_seed(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe, bool lb,
                       int32_t ub_seed, const Workspace& ws, cudaStream_t st, const Marker& mark,
                       float* seed_d = nullptr, int64_t* seed_i = nullptr) {
+    // The pair lists and work items (side stream) and the seed (caller's stream) both need only the
+    // probe lists, so they run side by side; the caller's stream then waits for the items.
     int rc_join = 0;
+    SideStream* ss = nullptr;
+    TB_TRY(side_stream(&ss), "side stream");
     const int G = scan_group_size(*idx, K);
     TB_TRY(mark(TRIDENT_PHASE_PAIRS), "event");
-    TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, 0, G, K, ws, st), "pairs");
-    TB_TRY(launch_item_order(*idx, B * nprobe, ws, st), "item order");
+    TB_TRY(cudaEventRecord(ss->fork2, st), "fork");
+    TB_TRY(cudaStreamWaitEvent(ss->s, ss->fork2, 0), "fork");
+    TB_TRY(launch_pairs(*idx, ws.probe, B, nprobe, 0, G, K, ws, ss->s), "pairs");
+    TB_TRY(launch_item_order(*idx, B * nprobe, ws, ss->s), "item order");
+    TB_TRY(cudaEventRecord(ss->join2, ss->s), "join");
     g_launches += 7;
     if ((rc_join = join_rotation(st))) return rc_join;  // qrot is read from here on
     if (lb) {
@@ -284,6 +294,7 @@ static int stage_seed(const trident_index* idx, const float* xq, int32_t B, int3
                "seed");
         g_launches += 1;
     }
+    TB_TRY(cudaStreamWaitEvent(st, ss->join2, 0), "join");
     return TRIDENT_OK;
 }
 
