@@ -82,7 +82,18 @@ class Dist:
 
             import torch.distributed as dist
 
-            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=self.dev)
+            # stdout carries exactly one JSON line: NCCL's version banner goes to stderr
+            os.environ.setdefault("NCCL_DEBUG", "WARN")
+            sys.stdout.flush()
+            saved = os.dup(1)
+            os.dup2(2, 1)
+            try:
+                dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=self.dev)
+                dist.barrier()
+            finally:
+                sys.stdout.flush()
+                os.dup2(saved, 1)
+                os.close(saved)
         return self
 
     def barrier(self):

@@ -83,6 +83,22 @@ class ShardedSearch:
 
         return merge_shards(d_all, i_all)
 
+    @staticmethod
+    def _pack(d, i):
+        """[n, k] float32 distances + [n, k] int64 ids -> one [n, 3k] int32 tensor."""
+        import torch
+
+        return torch.cat([d.contiguous().view(torch.int32), i.contiguous().view(torch.int32)], dim=1)
+
+    @staticmethod
+    def _unpack(p, R, n, k):
+        """[R * n, 3k] int32 -> ([R, n, k] float32, [R, n, k] int64), both contiguous."""
+        import torch
+
+        d = p[:, :k].contiguous().view(torch.float32).view(R, n, k)
+        i = p[:, k:].contiguous().view(torch.int64).view(R, n, k)
+        return d, i
+
     def _gather(self, t):
         import torch
         import torch.distributed as dist
@@ -108,24 +124,28 @@ class ShardedSearch:
         mark("coarse")
         probe, qrot, qinfo = self.index.search_prep(xq, nprobe)
         mark("gather")
-        xq_all, probe_all = self._gather(xq), self._gather(probe)
-        qrot_all, qinfo_all = self._gather(qrot), self._gather(qinfo)
+        # one all-gather of each query's [xq | q~ | qinfo | probe ids] as 32-bit words
+        D, Dp, Q = int(xq.shape[1]), int(qrot.shape[1]), int(qinfo.shape[1])
+        pack = torch.cat([xq.view(torch.int32), qrot.view(torch.int32), qinfo.view(torch.int32), probe], dim=1)
+        allp = self._gather(pack)
+        xq_all = allp[:, :D].contiguous().view(torch.float32)
+        qrot_all = allp[:, D:D + Dp].contiguous().view(torch.float32)
+        qinfo_all = allp[:, D + Dp:D + Dp + Q].contiguous().view(torch.float32)
+        probe_all = allp[:, D + Dp + Q:].contiguous()
         mark("seed")
         seed_d, seed_i = self.index.search_seed(xq_all, probe_all, qrot_all, qinfo_all, nprobe, k=k, mode=mode,
                                                 ub_seed=ub_seed)
         mark("tau")
-        sd_all = self._gather(seed_d).view(R, R * B, k)
-        si_all = self._gather(seed_i).view(R, R * B, k)
+        sd_all, si_all = self._unpack(self._gather(self._pack(seed_d, seed_i)), R, R * B, k)
         tau = self._merge(sd_all, si_all)[0][:, k - 1].contiguous()
         mark("scan")
         d_loc, i_loc = self.index.search_finish(xq_all, tau, nprobe, k=k, mode=mode, ub_seed=ub_seed)
         mark("exchange")
         # rank-major chunks of B queries: rank r receives chunk r of every rank -> [R, B, k]
-        d_in = torch.empty_like(d_loc)
-        i_in = torch.empty_like(i_loc)
-        dist.all_to_all_single(d_in, d_loc.contiguous(), group=self.group)
-        dist.all_to_all_single(i_in, i_loc.contiguous(), group=self.group)
-        d_in, i_in = d_in.view(R, B, k), i_in.view(R, B, k)
+        loc = self._pack(d_loc, i_loc)
+        inc = torch.empty_like(loc)
+        dist.all_to_all_single(inc, loc, group=self.group)
+        d_in, i_in = self._unpack(inc, R, B, k)
         mark("merge")
         out = self._merge(d_in, i_in)
         mark("end")
