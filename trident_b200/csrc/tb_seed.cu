@@ -24,6 +24,7 @@ constexpr int kSeedThreads = 256;
 constexpr int kSeedRowsMax = 8192;  // rows ranked per query: the first ones of its warm-up lists
 constexpr int kSeedBlocks = 2;      // leading 32-dim blocks used for the ranking
 constexpr int kSeedListsMax = 8;
+constexpr int kSeedBits = 12;       // key bits the selection resolves below the keys' common prefix
 
 struct SeedArgs {
     const float* xb;
@@ -72,11 +73,12 @@ __device__ __forceinline__ float ub_block_global(const uint4 w0, const uint4 w1,
     return acc;
 }
 
+// Callers alternate between two s_w buffers on consecutive calls: a buffer is written again two calls
+// later, after every thread has passed the barrier of the call in between and so has read it.
 __device__ __forceinline__ int block_sum(int v, int* s_w) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(TB_FULL, v, o);
-    __syncthreads();  // s_w may still be read by the previous call
     if (lane == 0) s_w[warp] = v;
     __syncthreads();
     int t = 0;
@@ -96,7 +98,8 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
     __shared__ int32_t s_off[kSeedListsMax + 1];
     __shared__ int32_t s_len[kSeedListsMax];
     __shared__ int64_t s_r0[kSeedListsMax], s_t0[kSeedListsMax];
-    __shared__ int s_w[kSeedThreads / 32];
+    __shared__ int s_w[2][kSeedThreads / 32];
+    __shared__ uint32_t s_mn[kSeedThreads / 32], s_mx[kSeedThreads / 32];
     __shared__ int s_n, s_valid;
 
     const int q = blockIdx.x;
@@ -164,6 +167,7 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
     }
     __syncthreads();
     // two rows per thread in flight: both rows' codes are loaded before either is evaluated
+    uint32_t kmin = 0xFFFFFFFFu, kmax = 0u;
     for (int i0 = tid; i0 < R; i0 += 2 * kSeedThreads) {
         uint4 cw[2][kSeedBlocks][2];
         int pp[2];
@@ -206,25 +210,54 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
                     acc = __ffma2_rn(e23, e23, acc);
                 }
             }
-            s_key[i] = __float_as_uint(acc.x + acc.y);  // non-negative: the bits order like the values
+            const uint32_t key = __float_as_uint(acc.x + acc.y);  // non-negative: the bits order like the values
+            s_key[i] = key;
+            kmin = min(kmin, key);
+            kmax = max(kmax, key);
         }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        kmin = min(kmin, __shfl_xor_sync(TB_FULL, kmin, o));
+        kmax = max(kmax, __shfl_xor_sync(TB_FULL, kmax, o));
+    }
+    if (lane == 0) {
+        s_mn[warp] = kmin;
+        s_mx[warp] = kmax;
     }
     __syncthreads();
 
-    // ---- select S rows: the S-th smallest key v by a bitwise search, then keys < v and enough == v
+    // ---- select S rows: every key below the bucket [v, v + 2^lo) that holds the S-th smallest key,
+    // then enough keys from inside it. The bits above the highest bit in which the smallest and the
+    // largest key differ are the same in every key; a bitwise search fixes the next kSeedBits bits.
+    // Which keys of the bucket are taken only changes how tight the threshold is: any S distinct rows
+    // bound the K-th distance from above.
     uint32_t v = 0xFFFFFFFFu;
+    int lo = 0;
     if (S < R) {
-        uint32_t pre = 0;
-        for (int bit = 30; bit >= 0; --bit) {
-            const uint32_t test = pre | ((1u << bit) - 1u);
-            int cnt = 0;
-            for (int i = tid; i < R; i += kSeedThreads) cnt += s_key[i] <= test;
-            if (block_sum(cnt, s_w) < S) pre |= 1u << bit;
+        uint32_t mn = s_mn[0], mx = s_mx[0];
+#pragma unroll
+        for (int w = 1; w < kSeedThreads / 32; ++w) {
+            mn = min(mn, s_mn[w]);
+            mx = max(mx, s_mx[w]);
+        }
+        uint32_t pre = mn;  // all keys equal: the bucket is that key
+        if (mn != mx) {
+            const int hb = 31 - __clz(mn ^ mx);
+            lo = max(0, hb + 1 - kSeedBits);
+            pre = mn & ~((2u << hb) - 1u);
+            for (int bit = hb; bit >= lo; --bit) {
+                const uint32_t test = pre | ((1u << bit) - 1u);
+                int cnt = 0;
+                for (int i = tid; i < R; i += kSeedThreads) cnt += s_key[i] <= test;
+                if (block_sum(cnt, s_w[bit & 1]) < S) pre |= 1u << bit;
+            }
         }
         v = pre;
     }
+    const uint32_t vb = v >> lo;
     for (int i = tid; i < R; i += kSeedThreads) {
-        if (s_key[i] < v || (v == 0xFFFFFFFFu)) {
+        if ((s_key[i] >> lo) < vb || (v == 0xFFFFFFFFu)) {
             const int k = atomicAdd(&s_n, 1);
             if (k < S) s_sel[k] = i;
         }
@@ -236,7 +269,7 @@ __global__ void __launch_bounds__(kSeedThreads, 4) seed_kernel(const SeedArgs a)
     __syncthreads();
     if (n_below < S) {
         for (int i = tid; i < R; i += kSeedThreads) {
-            if (s_key[i] == v) {
+            if ((s_key[i] >> lo) == vb) {
                 const int k = atomicAdd(&s_n, 1);
                 if (k < S) s_sel[k] = i;
             }
