@@ -174,9 +174,12 @@ __device__ __forceinline__ float2 scaled_group(const float2 c01, const float2 c2
 }
 
 constexpr int kNBS = 8;  // leading 32-dim blocks whose per-query base is staged in shared memory
+constexpr int kBS = 36;  // shared-memory stride of one 32-dim block (floats): 4 banks apart per block
 constexpr int kGC = 4;   // queries per CM-FP32 chunk: a chunk adds at most kGC * T survivors
 constexpr int kQM = 4;   // survivor-list capacity in units of T entries (>= kGC, >= the seed count)
 constexpr int kNBR = 1;  // code blocks a lane loads per deep-queue round (2 and 4 measured slower)
+constexpr int kWL = 32 * kQM;  // per-warp level-list capacity: the warps share the survivor list's space
+constexpr int kLevelMin = 12;  // a shorter level list continues in the deep queue
 
 // Survivor / deep-queue entry: query slot j (kJBits bits) and list-local row r (the rest).
 constexpr int kJBits = kMaxG <= 32 ? 5 : 6;
@@ -194,11 +197,14 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
     const int nb = a.nb;
     const int nbs = nb < kNBS ? nb : kNBS;  // staged blocks
     const int BW = nbs * 32;                // staged width per query
-    const int BWS = BW + 4;                 // its stride: rows of different queries start in different banks
+    // Shared-memory copies of per-dim data keep each 32-dim block kBS floats apart, so lanes at
+    // different blocks of the same dims read different banks; a query's row of bases is BWS floats
+    // long with BWS / 4 odd, so different queries start in different banks as well.
+    const int BWS = nbs * kBS + ((nbs & 1) ? 8 : 4);
     float* s_base = reinterpret_cast<float*>(smem);
     float* s_dl = s_base + (LB ? G * BWS : 0);
-    float* s_ep = s_dl + (LB ? D_pad : 0);
-    float* s_topd = s_ep + (LB ? D_pad : 0);
+    float* s_ep = s_dl + (LB ? nb * kBS : 0);
+    float* s_topd = s_ep + (LB ? nb * kBS : 0);
     int32_t* s_topi = reinterpret_cast<int32_t*>(s_topd + G * KM);
     uint32_t* s_sv = reinterpret_cast<uint32_t*>(s_topi + G * KM);  // [QCAP] survivors (j, r)
     float* s_sd = reinterpret_cast<float*>(s_sv + QCAP);            // [QCAP] their exact distances
@@ -253,8 +259,9 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
             const float4* d4 = reinterpret_cast<const float4*>(a.delta + (int64_t)c * D_pad);
             const float4* e4 = reinterpret_cast<const float4*>(a.eps + (int64_t)c * D_pad);
             for (int i = tid; i < D_pad / 4; i += T) {
-                reinterpret_cast<float4*>(s_dl)[i] = __ldg(d4 + i);
-                reinterpret_cast<float4*>(s_ep)[i] = __ldg(e4 + i);
+                const int o = (i >> 3) * (kBS / 4) + (i & 7);
+                reinterpret_cast<float4*>(s_dl)[o] = __ldg(d4 + i);
+                reinterpret_cast<float4*>(s_ep)[o] = __ldg(e4 + i);
             }
         }
         for (int i = tid; i < n * KM; i += T) {
@@ -270,7 +277,7 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 float4* b4 = reinterpret_cast<float4*>(s_base + j * BWS);
                 for (int i = lane; i < BW / 4; i += 32) {
                     const float4 x = __ldg(vm4 + i), y = __ldg(q4 + i);
-                    b4[i] = make_float4(x.x - y.x, x.y - y.y, x.z - y.z, x.w - y.w);
+                    b4[(i >> 3) * (kBS / 4) + (i & 7)] = make_float4(x.x - y.x, x.y - y.y, x.z - y.z, x.w - y.w);
                 }
             }
         }
@@ -332,12 +339,6 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
             __syncthreads();
         };
 
-        // push one survivor (j, r) (rare: per-thread atomics)
-        auto push_survivor = [&](int j, int r) {
-            const int p = atomicAdd(&s_sn, 1);
-            s_sv[p] = pack_jr(j, r);
-        };
-
         // ---- Stage X (optional): seed each query's threshold from SQ8 upper bounds of this list
         if (UB) {
             for (int t = 0; t < nt; ++t) {
@@ -354,10 +355,10 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                             for (int b = 0; b < nb; ++b) {
                                 uint4 w0, w1;
                                 load_block(tp + ((size_t)b * T + tid) * 32, w0, w1);
-                                acc = b < nbs ? ub_block(w0, w1, s_base + j * BWS + 32 * b, s_dl + 32 * b,
-                                                         s_ep + 32 * b, acc)
+                                acc = b < nbs ? ub_block(w0, w1, s_base + j * BWS + kBS * b, s_dl + kBS * b,
+                                                         s_ep + kBS * b, acc)
                                               : bound_block_g<true>(w0, w1, vm_c + 32 * b, qr + 32 * b,
-                                                                    s_dl + 32 * b, s_ep + 32 * b, acc);
+                                                                    s_dl + kBS * b, s_ep + kBS * b, acc);
                             }
                             ub = acc;
                         }
@@ -476,12 +477,13 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 const int j = i / (nsc * 4), d = i - j * (nsc * 4);
                 const int g = d >> 2, k = d & 3;
                 const float sc = s_scale[j];
-                const float b = s_base[j * BWS + d];
-                const float dl = s_dl[d];
+                const int sd = (d >> 5) * kBS + (d & 31);
+                const float b = s_base[j * BWS + sd];
+                const float dl = s_dl[sd];
                 float* P = s_sc + j * kSCS + g * 12;
                 P[k] = dl * sc;
                 P[4 + k] = b * sc;
-                P[8 + k] = (s_ep[d] * sc + 2.0001f * kU32 * sc * (255.0f * dl + fabsf(b))) * (1.0f + 3.0f * kU32);
+                P[8 + k] = (s_ep[sd] * sc + 2.0001f * kU32 * sc * (255.0f * dl + fabsf(b))) * (1.0f + 3.0f * kU32);
             }
             __syncthreads();
         }
@@ -504,6 +506,12 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
             float* wq_a = s_wqa + warp * kWQ;
             uint8_t* wq_b = s_wqb + warp * kWQ;
             int wq_n = 0;  // warp-uniform deep-queue fill
+            // the chunk's level list (rows alive after block 1, then after each further block), in the
+            // survivor-list space, which the CTA-wide refinement leaves unused during Stage Y/Z
+            float* wl_a = s_sd + warp * kWL;
+            uint8_t* wl_l = reinterpret_cast<uint8_t*>(s_sv) + warp * 2 * kWL;
+            uint8_t* wl_j = wl_l + kWL;
+            int wl_n = 0;  // warp-uniform fill
 
             // exact distance of list row r for query slot j (whole warp), insertion under the lock
             auto refine_one = [&](int j, int r) {
@@ -583,9 +591,9 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 for (int k = 0; k < kNBR; ++k) {
                     const int bb = b + sub + k * g;
                     if (bb < nb && part <= ts) {
-                        part = bb < nbs ? lb_block(w[k][0], w[k][1], s_base + j * BWS + 32 * bb, s_dl + 32 * bb, s_ep + 32 * bb, part)
+                        part = bb < nbs ? lb_block(w[k][0], w[k][1], s_base + j * BWS + kBS * bb, s_dl + kBS * bb, s_ep + kBS * bb, part)
                                         : bound_block_g<false>(w[k][0], w[k][1], vm_c + 32 * bb, qr + 32 * bb,
-                                                               s_dl + 32 * bb, s_ep + 32 * bb, part);
+                                                               s_dl + kBS * bb, s_ep + kBS * bb, part);
                         st_dims += 32u;
                     }
                 }
@@ -675,14 +683,25 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                             refine_one(__shfl_sync(TB_FULL, jj, s), __shfl_sync(TB_FULL, row, s));
                         }
                     } else if (m) {
-                        if (alive) {
-                            const int p = wq_n + __popc(m & ((1u << lane) - 1u));
-                            wq_e[p] = pack_jr(jj, row);
-                            wq_a[p] = acc * s_s2inv[jj];  // back to unscaled units
-                            wq_b[p] = 2;
+                        const int nm = __popc(m);
+                        const int p = __popc(m & ((1u << lane) - 1u));
+                        if (wl_n + nm <= kWL) {
+                            if (alive) {
+                                wl_l[wl_n + p] = (uint8_t)r;
+                                wl_j[wl_n + p] = (uint8_t)jj;
+                                wl_a[wl_n + p] = acc * s_s2inv[jj];  // back to unscaled units
+                            }
+                            __syncwarp();
+                            wl_n += nm;
+                        } else {
+                            if (alive) {
+                                wq_e[wq_n + p] = pack_jr(jj, row);
+                                wq_a[wq_n + p] = acc * s_s2inv[jj];
+                                wq_b[wq_n + p] = 2;
+                            }
+                            __syncwarp();
+                            wq_n += nm;
                         }
-                        __syncwarp();
-                        wq_n += __popc(m);
                     }
                     // move the unprocessed tail [cnt, wcnt) to the front
                     const int rest = wcnt - cnt;
@@ -735,6 +754,56 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 }
                 // the chunk's block-1 codes leave the registers: finish this warp's batch
                 if (wcnt > 0) run_batch(wcnt);
+                while (wq_n >= 32) deep_round(0);  // room for a short level list (< kLevelMin entries)
+                // Blocks 2, 3, ... for the chunk's level list, one block at a time: the block's codes of
+                // the chunk's 32 rows are loaded once (coalesced) and shuffled from the owning lane, and
+                // the list is compacted in place. A short list, and every row past the staged blocks,
+                // continues in the deep queue.
+                const int b_end = min(nbs, nb - 1);
+                int b = 2;
+                uint4 n0 = make_uint4(0, 0, 0, 0), n1 = make_uint4(0, 0, 0, 0);
+                if (valid && wl_n >= kLevelMin && b < b_end) load_block(tp + ((size_t)b * T + lane) * 32, n0, n1);
+                for (; wl_n >= kLevelMin && b < b_end; ++b) {
+                    const uint4 c0 = n0, c1 = n1;
+                    if (valid && b + 1 < b_end) load_block(tp + ((size_t)(b + 1) * T + lane) * 32, n0, n1);
+                    int wn = 0;
+                    for (int k0 = 0; k0 < wl_n; k0 += 32) {
+                        const bool has = k0 + lane < wl_n;
+                        const int r = has ? wl_l[k0 + lane] : 0;
+                        const int jj = has ? wl_j[k0 + lane] : 0;
+                        float acc = has ? wl_a[k0 + lane] : 0.0f;
+                        const uint4 w0 = make_uint4(__shfl_sync(TB_FULL, c0.x, r), __shfl_sync(TB_FULL, c0.y, r),
+                                                    __shfl_sync(TB_FULL, c0.z, r), __shfl_sync(TB_FULL, c0.w, r));
+                        const uint4 w1 = make_uint4(__shfl_sync(TB_FULL, c1.x, r), __shfl_sync(TB_FULL, c1.y, r),
+                                                    __shfl_sync(TB_FULL, c1.z, r), __shfl_sync(TB_FULL, c1.w, r));
+                        acc = lb_block(w0, w1, s_base + jj * BWS + kBS * b, s_dl + kBS * b, s_ep + kBS * b, acc);
+                        if (has) st_dims += 32u;
+                        const bool alive = has && acc <= s_ts[jj];
+                        const unsigned m = __ballot_sync(TB_FULL, alive);
+                        __syncwarp();  // every entry of this batch is read before survivors overwrite
+                        if (alive) {
+                            const int p = wn + __popc(m & ((1u << lane) - 1u));
+                            wl_l[p] = (uint8_t)r;
+                            wl_j[p] = (uint8_t)jj;
+                            wl_a[p] = acc;
+                        }
+                        wn += __popc(m);
+                        __syncwarp();
+                    }
+                    wl_n = wn;
+                }
+                for (int k0 = 0; k0 < wl_n; k0 += 32) {  // the rest continues at block b
+                    const int cnt = min(32, wl_n - k0);
+                    if (lane < cnt) {
+                        wq_e[wq_n + lane] = pack_jr(wl_j[k0 + lane], rb + wl_l[k0 + lane]);
+                        wq_a[wq_n + lane] = wl_a[k0 + lane];
+                        wq_b[wq_n + lane] = (uint8_t)b;
+                    }
+                    __syncwarp();
+                    wq_n += cnt;
+                    while (wq_n >= 32) deep_round(0);
+                }
+                wl_n = 0;
                 while (wq_n >= 32) deep_round(0);
             }
             // drain the deep queue, giving each remaining entry as many lanes as fit
@@ -875,7 +944,8 @@ static size_t scan_smem(const trident_index& idx, int K, int G, bool lb) {
     const int nbs = idx.num_blocks < kNBS ? idx.num_blocks : kNBS;
     const size_t qcap = (size_t)kQM * T;
     size_t s = 0;
-    if (lb) s += ((size_t)G * (nbs * 32 + 4) + 2 * (size_t)idx.D_pad) * sizeof(float);  // base, delta, eps
+    const size_t bws = (size_t)nbs * kBS + ((nbs & 1) ? 8 : 4);
+    if (lb) s += ((size_t)G * bws + 2 * (size_t)idx.num_blocks * kBS) * sizeof(float);  // base, delta, eps
     s += (size_t)G * KM * (sizeof(float) + sizeof(int32_t));                          // top-K lists
     s += qcap * (sizeof(uint32_t) + sizeof(float));                                   // survivors + distances
     if (lb) s += (size_t)G * kSCS * sizeof(float);                                    // scaled intervals
