@@ -107,12 +107,15 @@ __device__ __forceinline__ void unpack_block(const uint4 w0, const uint4 w1, flo
         for (int k = 0; k < 4; ++k) cf[4 * i + k] = u8f(w[i], k);
 }
 
-// Stage Y on one block whose codes are already floats.
-__device__ __forceinline__ float lb_block_f(const float* cf, const float* __restrict__ base,
+// Stage Y on block 0 whose codes are already floats; base = vmin - q~ is formed from global memory
+// with the same float32 subtraction as the shared-memory copies.
+__device__ __forceinline__ float lb_block_f(const float* cf, const float* __restrict__ vm, const float* __restrict__ qr,
                                             const float* __restrict__ dl, const float* __restrict__ ep, float acc) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float4 b4 = *reinterpret_cast<const float4*>(base + 4 * i);
+        const float4 v4 = __ldg(reinterpret_cast<const float4*>(vm) + i);
+        const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr) + i);
+        const float4 b4 = make_float4(v4.x - q4.x, v4.y - q4.y, v4.z - q4.z, v4.w - q4.w);
         const float4 d4 = *reinterpret_cast<const float4*>(dl + 4 * i);
         const float4 e4 = *reinterpret_cast<const float4*>(ep + 4 * i);
         float l;
@@ -173,8 +176,9 @@ __device__ __forceinline__ float2 scaled_group(const float2 c01, const float2 c2
     return __ffma2_rn(make_float2(l2, l3), make_float2(l2, l3), acc);
 }
 
-constexpr int kNBS = 8;  // leading 32-dim blocks whose per-query base is staged in shared memory
+constexpr int kNBS = 16;  // blocks [kB0, kNBS) have a per-query base staged in shared memory
 constexpr int kBS = 36;  // shared-memory stride of one 32-dim block (floats): 4 banks apart per block
+constexpr int kB0 = 2;   // first block with a per-query base in shared memory (blocks 0-1 use the scaled form)
 constexpr int kGC = 4;   // queries per CM-FP32 chunk: a chunk adds at most kGC * T survivors
 constexpr int kQM = 4;   // survivor-list capacity in units of T entries (>= kGC, >= the seed count)
 constexpr int kNBR = 1;  // code blocks a lane loads per deep-queue round (2 and 4 measured slower)
@@ -196,11 +200,11 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
     const int D_pad = a.D_pad;
     const int nb = a.nb;
     const int nbs = nb < kNBS ? nb : kNBS;  // staged blocks
-    const int BW = nbs * 32;                // staged width per query
+    const int nsb = nbs > kB0 ? nbs - kB0 : 0;  // blocks kB0 .. nbs-1 have a per-query base in smem
     // Shared-memory copies of per-dim data keep each 32-dim block kBS floats apart, so lanes at
     // different blocks of the same dims read different banks; a query's row of bases is BWS floats
     // long with BWS / 4 odd, so different queries start in different banks as well.
-    const int BWS = nbs * kBS + ((nbs & 1) ? 8 : 4);
+    const int BWS = nsb * kBS + ((nsb & 1) ? 8 : 4);
     float* s_base = reinterpret_cast<float*>(smem);
     float* s_dl = s_base + (LB ? G * BWS : 0);
     float* s_ep = s_dl + (LB ? nb * kBS : 0);
@@ -271,11 +275,11 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
         __syncthreads();
         if (LB) {
             // base_j = vmin_c - q~_j on the staged blocks, one warp per query, float4 over dims
-            const float4* vm4 = reinterpret_cast<const float4*>(vm_c);
+            const float4* vm4 = reinterpret_cast<const float4*>(vm_c + 32 * kB0);
             for (int j = warp; j < n; j += NW) {
-                const float4* q4 = reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad);
+                const float4* q4 = reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad + 32 * kB0);
                 float4* b4 = reinterpret_cast<float4*>(s_base + j * BWS);
-                for (int i = lane; i < BW / 4; i += 32) {
+                for (int i = lane; i < nsb * 8; i += 32) {
                     const float4 x = __ldg(vm4 + i), y = __ldg(q4 + i);
                     b4[(i >> 3) * (kBS / 4) + (i & 7)] = make_float4(x.x - y.x, x.y - y.y, x.z - y.z, x.w - y.w);
                 }
@@ -355,8 +359,9 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                             for (int b = 0; b < nb; ++b) {
                                 uint4 w0, w1;
                                 load_block(tp + ((size_t)b * T + tid) * 32, w0, w1);
-                                acc = b < nbs ? ub_block(w0, w1, s_base + j * BWS + kBS * b, s_dl + kBS * b,
-                                                         s_ep + kBS * b, acc)
+                                acc = (b >= kB0 && b < nbs)
+                                          ? ub_block(w0, w1, s_base + j * BWS + kBS * (b - kB0), s_dl + kBS * b,
+                                                     s_ep + kBS * b, acc)
                                               : bound_block_g<true>(w0, w1, vm_c + 32 * b, qr + 32 * b,
                                                                     s_dl + kBS * b, s_ep + kBS * b, acc);
                             }
@@ -419,7 +424,8 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                         const int je = min(n, jc + kQM);
                         for (int j = jc; j < je; ++j)
                             if (s_seed[j])
-                                s_sd[(j - jc) * T + tid] = v < L ? lb_block_f(cf, s_base + j * BWS, s_dl, s_ep, 0.0f) : kInf;
+                                s_sd[(j - jc) * T + tid] =
+                                    v < L ? lb_block_f(cf, vm_c, a.qrot + (int64_t)s_qid[j] * D_pad, s_dl, s_ep, 0.0f) : kInf;
                         __syncthreads();
                         for (int j = jc + warp; j < je; j += NW) {
                             if (!s_seed[j]) continue;
@@ -478,7 +484,7 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 const int g = d >> 2, k = d & 3;
                 const float sc = s_scale[j];
                 const int sd = (d >> 5) * kBS + (d & 31);
-                const float b = s_base[j * BWS + sd];
+                const float b = __ldg(vm_c + d) - __ldg(a.qrot + (int64_t)s_qid[j] * D_pad + d);  // as staged
                 const float dl = s_dl[sd];
                 float* P = s_sc + j * kSCS + g * 12;
                 P[k] = dl * sc;
@@ -591,7 +597,8 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 for (int k = 0; k < kNBR; ++k) {
                     const int bb = b + sub + k * g;
                     if (bb < nb && part <= ts) {
-                        part = bb < nbs ? lb_block(w[k][0], w[k][1], s_base + j * BWS + kBS * bb, s_dl + kBS * bb, s_ep + kBS * bb, part)
+                        part = bb < nbs ? lb_block(w[k][0], w[k][1], s_base + j * BWS + kBS * (bb - kB0), s_dl + kBS * bb,
+                                                   s_ep + kBS * bb, part)
                                         : bound_block_g<false>(w[k][0], w[k][1], vm_c + 32 * bb, qr + 32 * bb,
                                                                s_dl + kBS * bb, s_ep + kBS * bb, part);
                         st_dims += 32u;
@@ -776,7 +783,7 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                                                     __shfl_sync(TB_FULL, c0.z, r), __shfl_sync(TB_FULL, c0.w, r));
                         const uint4 w1 = make_uint4(__shfl_sync(TB_FULL, c1.x, r), __shfl_sync(TB_FULL, c1.y, r),
                                                     __shfl_sync(TB_FULL, c1.z, r), __shfl_sync(TB_FULL, c1.w, r));
-                        acc = lb_block(w0, w1, s_base + jj * BWS + kBS * b, s_dl + kBS * b, s_ep + kBS * b, acc);
+                        acc = lb_block(w0, w1, s_base + jj * BWS + kBS * (b - kB0), s_dl + kBS * b, s_ep + kBS * b, acc);
                         if (has) st_dims += 32u;
                         const bool alive = has && acc <= s_ts[jj];
                         const unsigned m = __ballot_sync(TB_FULL, alive);
@@ -944,7 +951,8 @@ static size_t scan_smem(const trident_index& idx, int K, int G, bool lb) {
     const int nbs = idx.num_blocks < kNBS ? idx.num_blocks : kNBS;
     const size_t qcap = (size_t)kQM * T;
     size_t s = 0;
-    const size_t bws = (size_t)nbs * kBS + ((nbs & 1) ? 8 : 4);
+    const int nsb = nbs > kB0 ? nbs - kB0 : 0;
+    const size_t bws = (size_t)nsb * kBS + ((nsb & 1) ? 8 : 4);
     if (lb) s += ((size_t)G * bws + 2 * (size_t)idx.num_blocks * kBS) * sizeof(float);  // base, delta, eps
     s += (size_t)G * KM * (sizeof(float) + sizeof(int32_t));                          // top-K lists
     s += qcap * (sizeof(uint32_t) + sizeof(float));                                   // survivors + distances
