@@ -228,9 +228,13 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
     const int K = a.K, D = a.D;
     unsigned long long st_cand = 0, st_dims = 0, st_surv = 0, st_ins = 0, st_items = 0;
 
+    // Items are claimed one ahead: thread 0 holds the next item's index in a register, so the claim's
+    // atomic round trip overlaps the current item.
+    int next_item = tid == 0 ? atomicAdd(a.work_ctr, 1) : 0;
     for (;;) {
         if (tid == 0) {
-            s_item = atomicAdd(a.work_ctr, 1);
+            s_item = next_item;
+            next_item = atomicAdd(a.work_ctr, 1);
             s_sn = 0;
             s_chunk = 0;
         }
@@ -274,15 +278,16 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
         }
         __syncthreads();
         if (LB) {
-            // base_j = vmin_c - q~_j on the staged blocks, one warp per query, float4 over dims
+            // base_j = vmin_c - q~_j on the staged blocks, float4 over dims, four loads in flight per thread
             const float4* vm4 = reinterpret_cast<const float4*>(vm_c + 32 * kB0);
-            for (int j = warp; j < n; j += NW) {
-                const float4* q4 = reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad + 32 * kB0);
-                float4* b4 = reinterpret_cast<float4*>(s_base + j * BWS);
-                for (int i = lane; i < nsb * 8; i += 32) {
-                    const float4 x = __ldg(vm4 + i), y = __ldg(q4 + i);
-                    b4[(i >> 3) * (kBS / 4) + (i & 7)] = make_float4(x.x - y.x, x.y - y.y, x.z - y.z, x.w - y.w);
-                }
+            const int per = nsb * 8, tot = n * per;
+#pragma unroll 4
+            for (int i = tid; i < tot; i += T) {
+                const int j = i / per, f = i - j * per;
+                const float4 x = __ldg(vm4 + f);
+                const float4 y = __ldg(reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad + 32 * kB0) + f);
+                reinterpret_cast<float4*>(s_base + j * BWS)[(f >> 3) * (kBS / 4) + (f & 7)] =
+                    make_float4(x.x - y.x, x.y - y.y, x.z - y.z, x.w - y.w);
             }
         }
         __syncthreads();
@@ -479,17 +484,29 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 s_tsp[tid] = (ts < kInf) ? ts * sc * sc * (1.0f + 64.0f * kU32) : kInf;
             }
             __syncthreads();
-            for (int i = tid; i < n * nsc * 4; i += T) {
-                const int j = i / (nsc * 4), d = i - j * (nsc * 4);
-                const int g = d >> 2, k = d & 3;
+            // one 4-dim group per task; base = vmin - q~ with the same float32 subtraction as the staged copies
+#pragma unroll 2
+            for (int i = tid; i < n * nsc; i += T) {
+                const int j = i / nsc, g = i - j * nsc;
                 const float sc = s_scale[j];
-                const int sd = (d >> 5) * kBS + (d & 31);
-                const float b = __ldg(vm_c + d) - __ldg(a.qrot + (int64_t)s_qid[j] * D_pad + d);  // as staged
-                const float dl = s_dl[sd];
-                float* P = s_sc + j * kSCS + g * 12;
-                P[k] = dl * sc;
-                P[4 + k] = b * sc;
-                P[8 + k] = (s_ep[sd] * sc + 2.0001f * kU32 * sc * (255.0f * dl + fabsf(b))) * (1.0f + 3.0f * kU32);
+                const int sd = (g >> 3) * kBS + 4 * (g & 7);
+                const float4 v4 = __ldg(reinterpret_cast<const float4*>(vm_c) + g);
+                const float4 q4 = __ldg(reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad) + g);
+                const float4 d4 = *reinterpret_cast<const float4*>(s_dl + sd);
+                const float4 e4 = *reinterpret_cast<const float4*>(s_ep + sd);
+                const float b[4] = {v4.x - q4.x, v4.y - q4.y, v4.z - q4.z, v4.w - q4.w};
+                const float dl[4] = {d4.x, d4.y, d4.z, d4.w}, ep[4] = {e4.x, e4.y, e4.z, e4.w};
+                float o[12];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    o[k] = dl[k] * sc;
+                    o[4 + k] = b[k] * sc;
+                    o[8 + k] = (ep[k] * sc + 2.0001f * kU32 * sc * (255.0f * dl[k] + fabsf(b[k]))) * (1.0f + 3.0f * kU32);
+                }
+                float4* P = reinterpret_cast<float4*>(s_sc + j * kSCS + g * 12);
+                P[0] = make_float4(o[0], o[1], o[2], o[3]);
+                P[1] = make_float4(o[4], o[5], o[6], o[7]);
+                P[2] = make_float4(o[8], o[9], o[10], o[11]);
             }
             __syncthreads();
         }
