@@ -588,9 +588,11 @@ def run_reference(args, d: Dist):
     return {
         "metric": METRIC, "value": round(qps, 2), "unit": UNIT, "n_gpus": d.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(tot / args.steps * 1e3, 2), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": {"workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} nprobe={cfg.nprobe} "
-                               f"K={cfg.K} B={cfg.B}", "sample_queries_per_step": n},
+                               f"K={cfg.K} B={cfg.B} per GPU", "global_batch": cfg.B * d.world,
+                   "host": "rank 0's host cores only: the reference's CPU path does not use the GPUs",
+                   "sample_queries_per_step": n},
         "cpu_baseline": {"value": round(qps, 2), "unit": UNIT, "cores": threads, "kind": "reference",
                          "sample": f"each step: first {n} queries, float64 probe selection + omp_cpu_ivfflat_f32"},
         "e2e": {"value": round(qps, 2), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
