@@ -6,10 +6,12 @@ nprobe=64, K=10, B=1000 queries; synthetic GIST1M-shaped rows (|N(0,1)| (d+1)^-0
 generated on the GPU from fixed seeds (the real dataset is not used). The cost router picks the
 cascade for this workload. With --gpus N the IVF lists are sharded across N ranks (one process
 per GPU) and every rank brings its own B queries. A step runs over the N * B queries:
-  - all-gather of the probe lists over NCCL;
-  - min-all-reduce of the thresholds;
+  - each rank runs the coarse stage for its own queries; one NCCL all-gather shares the queries,
+    rotated queries, side information and probe lists;
+  - each rank seeds every query from its own lists; an all-gather of the seed lists and a device
+    merge give each query's threshold;
   - each rank scans its own lists;
-  - all-to-all of the per-rank top-K lists and a device merge.
+  - an all-to-all of the per-rank top-K lists and a device merge.
 Per-GPU work stays fixed, so the bench reports "weak" scaling.
 
 One step = one search of the batch. `value` = N * B / step time with the queries already in HBM
