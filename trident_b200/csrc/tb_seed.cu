@@ -22,7 +22,7 @@ namespace tb {
 
 constexpr int kSeedThreads = 256;
 constexpr int kSeedRowsMax = 8192;  // rows ranked per query: the first ones of its warm-up lists
-constexpr int kSeedBlocks = 2;      // leading 32-dim blocks used for the ranking
+constexpr int kSeedBlocks = 1;      // leading 32-dim blocks used for the ranking
 constexpr int kSeedListsMax = 8;
 constexpr int kSeedBits = 12;       // key bits the selection resolves below the keys' common prefix
 
