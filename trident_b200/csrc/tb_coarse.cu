@@ -191,7 +191,8 @@ cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, floa
 constexpr int kSelThreads = 256;
 constexpr int kSelNW = kSelThreads / 32;
 constexpr int kSelCap = 2048;        // sorted best (<= nprobe <= 1024) + one batch of re-check members
-constexpr int kSelSmemKeys = 8192;   // approximate distances cached in shared memory up to this nlist
+constexpr int kSelSmemKeys = 8192;
+constexpr int kSelRegKeys = 4;      // keys per thread held in registers by the threshold search (nlist <= 1024)   // approximate distances cached in shared memory up to this nlist
 
 __device__ void bitonic_sort_kc(unsigned long long* key, int32_t* cid, int P) {
     for (int k = 2; k <= P; k <<= 1) {
@@ -254,6 +255,42 @@ __device__ __forceinline__ double l2_f64_warp(const float* __restrict__ qv, cons
     return total;
 }
 
+// Two rows at once, each in exactly the order of l2_f64_warp (two independent fma chains).
+__device__ __forceinline__ void l2_f64_warp2(const float* __restrict__ qv, const float* __restrict__ ca,
+                                             const float* __restrict__ cb, int D, int lane, double& ra, double& rb) {
+    double aa = 0.0, ab = 0.0;
+    int d = lane;
+    for (; d + 96 < D; d += 128) {
+        float a4[4], b4[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            a4[u] = __ldg(ca + d + 32 * u);
+            b4[u] = __ldg(cb + d + 32 * u);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const double q = (double)qv[d + 32 * u];
+            const double da = q - (double)a4[u], db = q - (double)b4[u];
+            aa = fma(da, da, aa);
+            ab = fma(db, db, ab);
+        }
+    }
+    for (; d < D; d += 32) {
+        const double q = (double)qv[d];
+        const double da = q - (double)__ldg(ca + d), db = q - (double)__ldg(cb + d);
+        aa = fma(da, da, aa);
+        ab = fma(db, db, ab);
+    }
+    double ta = __shfl_sync(TB_FULL, aa, 0), tb = __shfl_sync(TB_FULL, ab, 0);
+#pragma unroll
+    for (int l = 1; l < 32; ++l) {
+        ta += __shfl_sync(TB_FULL, aa, l);
+        tb += __shfl_sync(TB_FULL, ab, l);
+    }
+    ra = ta;
+    rb = tb;
+}
+
 __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
     const float* __restrict__ coarse, const float* __restrict__ xq, const float* __restrict__ cent,
     const float* __restrict__ qinfo, int nlist, int D, int nprobe, float cmax, int32_t* __restrict__ probe,
@@ -277,15 +314,34 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
     // 1) the nprobe-th smallest approximate value, bit by bit from the top: bit b of the answer is
     //    0 iff at least nprobe keys are <= (answer so far with bit b = 0 and all lower bits = 1)
     uint32_t ans = 0;
-    for (int b = 31; b >= 0; --b) {
-        const uint32_t upper = ans | ((1u << b) - 1u);
-        int cnt = 0;
-        for (int c = tid; c < nlist; c += blockDim.x) {
-            const uint32_t k = cached ? skeys[c] : float_key(__ldg(row + c));
-            cnt += k <= upper;
+    if (nlist <= kSelRegKeys * kSelThreads) {  // this thread's keys in registers (absent: all ones)
+        uint32_t kr[kSelRegKeys];
+#pragma unroll
+        for (int u = 0; u < kSelRegKeys; ++u) {
+            const int c = tid + u * kSelThreads;
+            kr[u] = c < nlist ? (cached ? skeys[c] : float_key(__ldg(row + c))) : 0xFFFFFFFFu;
         }
-        cnt = block_sum_sel(cnt, red);
-        if (cnt < nprobe) ans |= (1u << b);
+        const int pad = kSelRegKeys * kSelThreads - nlist;  // padding keys count as <= upper only at 0xFFFFFFFF
+        for (int b = 31; b >= 0; --b) {
+            const uint32_t upper = ans | ((1u << b) - 1u);
+            int cnt = 0;
+#pragma unroll
+            for (int u = 0; u < kSelRegKeys; ++u) cnt += kr[u] <= upper;
+            cnt = block_sum_sel(cnt, red);
+            if (upper == 0xFFFFFFFFu) cnt -= pad;
+            if (cnt < nprobe) ans |= (1u << b);
+        }
+    } else {
+        for (int b = 31; b >= 0; --b) {
+            const uint32_t upper = ans | ((1u << b) - 1u);
+            int cnt = 0;
+            for (int c = tid; c < nlist; c += blockDim.x) {
+                const uint32_t k = cached ? skeys[c] : float_key(__ldg(row + c));
+                cnt += k <= upper;
+            }
+            cnt = block_sum_sel(cnt, red);
+            if (cnt < nprobe) ans |= (1u << b);
+        }
     }
     const float t = key_float(ans);
 
@@ -305,10 +361,20 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
     long long members = 0;
     auto process_batch = [&]() {
         // exact float64 distance of each batch member (one warp per member), then sort best + batch
-        for (int i = warp; i < batch; i += kSelNW) {
+        for (int i = warp; i < batch; i += 2 * kSelNW) {
+            const int i2 = i + kSelNW;
             const int c = scid[best_n + i];
-            const double d64 = l2_f64_warp(qv, cent + (int64_t)c * D, D, lane);
-            if (lane == 0) skey[best_n + i] = (unsigned long long)__double_as_longlong(d64);
+            if (i2 < batch) {
+                double da, db;
+                l2_f64_warp2(qv, cent + (int64_t)c * D, cent + (int64_t)scid[best_n + i2] * D, D, lane, da, db);
+                if (lane == 0) {
+                    skey[best_n + i] = (unsigned long long)__double_as_longlong(da);
+                    skey[best_n + i2] = (unsigned long long)__double_as_longlong(db);
+                }
+            } else {
+                const double d64 = l2_f64_warp(qv, cent + (int64_t)c * D, D, lane);
+                if (lane == 0) skey[best_n + i] = (unsigned long long)__double_as_longlong(d64);
+            }
         }
         const int n = best_n + batch;
         int P = 1;
