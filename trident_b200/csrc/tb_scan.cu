@@ -512,12 +512,15 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
         }
 
         if (LB) {
-            // ---- Stage Y/Z, warp-independent within the item. Each warp owns 32 rows of every tile:
+            // ---- Stage Y/Z, warp-independent within the item. Each warp takes 32-row chunks of the list:
             //  * block 0 for every query of the item, full warps, codes as floats in registers;
             //  * rows alive after block 0 are batched per warp; their block 1 runs densely with the
             //    codes shuffled from the owning lane;
-            //  * rows alive after block 1 go to the warp's deep queue, advanced one block per lane per
-            //    round (entries at mixed levels), so a round's load latency overlaps other warps' work;
+            //  * rows alive after block 1 go to the warp's level list, which advances one block at a
+            //    time over the chunk when the warp leaves it (blocks 2 .. kNBS-1, codes loaded once
+            //    per chunk and block);
+            //  * a short level list, and rows past the staged blocks, go to the warp's deep queue,
+            //    advanced one block per lane per round (entries at mixed levels);
             //  * a row that survives every block is refined at once by its warp (exact FP32, reference
             //    order) and inserted into its query's top-K under a per-query lock; the query's
             //    threshold tightens immediately for every warp.
