@@ -588,11 +588,11 @@ def run_reference(args, d: Dist):
     tot = sum(times)
     qps = n * args.steps / tot
     return {
-        "metric": METRIC, "value": round(qps, 2), "unit": UNIT, "n_gpus": d.world, "steps": args.steps,
+        "metric": METRIC, "value": round(qps, 2), "unit": UNIT, "n_gpus": getattr(d, "launched", d.world), "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(tot / args.steps * 1e3, 2), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": {"workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} nprobe={cfg.nprobe} "
-                               f"K={cfg.K} B={cfg.B} per GPU", "global_batch": cfg.B * d.world,
+                               f"K={cfg.K} B={cfg.B} per GPU", "global_batch": cfg.B * getattr(d, "launched", d.world),
                    "host": "rank 0's host cores only: the reference's CPU path does not use the GPUs",
                    "sample_queries_per_step": n},
         "cpu_baseline": {"value": round(qps, 2), "unit": UNIT, "cores": threads, "kind": "reference",
@@ -608,6 +608,7 @@ def main():
         # the CPU reference runs on rank 0 alone; other ranks exit without work
         if d.rank != 0:
             return 0
+        d.launched = d.world  # the job's GPU count, reported; rank 0 alone runs, without a process group
         d.world = 1
     d.init()
     try:
