@@ -127,9 +127,10 @@ int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, doubl
  *            argument);
  *   out_d    [B, K] float32 squared distances ascending; out_i [B, K] int64 original ids;
  *            ties are broken by the smaller id; missing results are (+inf, -1). Every row
- *            reads (NaN, -2) if a bounded wait inside the scan gave up, since a candidate may
- *            then be missing (not expected in normal operation; the call still returns 0
- *            because the check runs on the device after the launch);
+ *            reads (NaN, -2) if a bounded wait inside the coarse GEMM or the scan gave up, since
+ *            a probe or a candidate may then be missing (not expected in normal operation; the
+ *            call still returns 0 because the check runs on the device after the launch, and
+ *            trident_workspace_status reads the reason);
  *   stats    optional int64[TRIDENT_STATS_LEN] accumulated counters (NULL to skip). */
 int trident_search(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
                    int32_t mode, int32_t ub_seed, void* workspace, size_t workspace_bytes,
@@ -156,6 +157,29 @@ int trident_search_profiled(const trident_index* idx, const float* xq, int32_t B
 /* Number of kernels the library has launched from the calling thread so far. */
 int64_t trident_launch_count(void);
 
+/* Device-side status of the last search that used a workspace (no counterpart in the reference,
+ * whose kernels had no bounded waits and reported nothing). Every wait inside the kernels is
+ * bounded; a wait that gives up records why in a status word of the workspace, and the results it
+ * may have spoiled read (NaN, -2) (probe lists: -1). */
+enum trident_device_status {
+    TRIDENT_STATUS_OK = 0,
+    TRIDENT_STATUS_LOCK_TIMEOUT = 1,  /* the scan gave up on a per-query insertion lock         */
+    TRIDENT_STATUS_MMA_TIMEOUT = 2    /* the coarse GEMM gave up waiting for its tensor-core MMAs */
+};
+
+/* Waits for `stream`, then reads the status word of `workspace` (the buffer last passed to
+ * trident_search / trident_coarse / trident_search_prep / _seed / _finish) into *status: a bitwise
+ * OR of TRIDENT_STATUS_* values. The word sits at the start of the workspace, so no sizes are
+ * needed. In the staged multi-GPU search the status of a query's coarse stage travels with its
+ * qinfo row, so finish's workspace reports a GEMM timeout on any rank. */
+int trident_workspace_status(const void* workspace, void* stream, int32_t* status);
+
+/* Limits of the bounded waits, process-wide: lock_spins tries of a per-query insertion lock (default
+ * 2^22, each followed by a 64 ns sleep) and mma_polls polls of a tensor-core completion barrier
+ * (default 2^22). A negative value restores the default. A limit of 0 makes every such wait give
+ * up at once, which is how the tests exercise the error path without a GPU fault. */
+int trident_set_wait_limits(int64_t lock_spins, int64_t mma_polls);
+
 /* The coarse stage alone (query PCA rotation + exact top-nprobe list selection), replacing the
  * addmm_out + trident_topk_centroids_kernel pair (:1233-1259). probe_cids [B, nprobe] int32 comes
  * out ascending by (float64 ||q - c||^2, list id); probe_d64 [B, nprobe] (optional) holds those
@@ -172,12 +196,18 @@ int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t
  * trident_search without the workspace: the workspace is a TRIDENT_NOALLOC_WORKSPACE_BYTES array
  * compiled into the library, held by every GPU that loads it until the process exits. Returns
  * TRIDENT_ERR_WORKSPACE when trident_workspace_size(B, K, nprobe) exceeds that size. No call
- * allocates. All calls on a device share the array: calls whose GPU work overlaps in time race
- * and must be serialised by the caller. The first call on each device looks up the array's
- * device address; make it before capturing a stream. */
+ * allocates device memory. All calls on a device share the array: calls whose GPU work overlaps in
+ * time race and must be serialised by the caller. The first call on each device looks up the
+ * array's device address, and the first search from each host thread on each device creates the
+ * library's side stream and its four events (as trident_search does); make that first call before
+ * capturing a stream. */
 int trident_search_noalloc(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
                            int32_t mode, int32_t ub_seed, float* out_d, int64_t* out_i, int64_t* stats,
                            void* stream);
+
+/* TRIDENT_NOALLOC_WORKSPACE_BYTES as compiled into the library (for bindings that cannot read the
+ * header's macro). */
+size_t trident_noalloc_workspace_bytes(void);
 
 /* Per-query side information of trident_search_prep: [B, TRIDENT_QINFO_LEN] float32 (||q||,
  * the bound's query slack sigma, ||q - mu||, padding). */
@@ -215,7 +245,8 @@ int trident_search_finish(const trident_index* idx, const float* xq_all, int32_t
                           int64_t* stats, void* stream);
 
 /* Multi-GPU merge: R per-shard result lists d_in/i_in [R, B, K] (as gathered by an NCCL
- * all-gather) -> the global top-K per query under the (distance, id) order. */
+ * all-gather) -> the global top-K per query under the (distance, id) order. A query for which any
+ * shard reports an id of -2 (a bounded wait gave up there) comes out as (NaN, -2) in every slot. */
 int trident_merge_shards(const float* d_in, const int64_t* i_in, int32_t R, int32_t B, int32_t K,
                          float* out_d, int64_t* out_i, void* stream);
 

@@ -9,8 +9,10 @@ host core, so that the baseline uses the box's cores instead of 24.
 
 Nothing is copied into the repository: the extracted source and the built module are written only
 under oracle/_ref/, which git ignores. The module is built twice (x86-64-v3 and x86-64-v4) because
-the GPU box's host CPU is not known here; ref_cpu.py loads the one the running CPU supports.
-Only runs where /root/reference exists (this container); the GPU box uses the prebuilt files.
+the host CPU that will run it is not known at build time; ref_cpu.py loads the one the running CPU
+supports.
+It runs only where the reference checkout is present (TRIDENT_REFERENCE_ROOT, else a `reference`
+directory beside the repository root); machines without it use the prebuilt files.
 """
 import os
 import re
@@ -18,7 +20,8 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT = os.path.join(HERE, "_ref")
-REF_ROOT = os.environ.get("TRIDENT_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("TRIDENT_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 REF_FILE = os.path.join(REF_ROOT, "benchmarks", "phase8_ooc_100m_4080.py")
 LEVELS = {"x86-64-v3": "trident_ref_cpu_v3", "x86-64-v4": "trident_ref_cpu_v4"}
 

@@ -1,7 +1,7 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Runs only where the reference is mounted (this build container); the GPU box uses the committed
-.npz files. For each case it:
+Runs only where the reference checkout is present (see oracle/ref_build.py); other machines use the
+committed .npz files. For each case it:
   1. draws a small seeded dataset with trident_b200.datasets (NumPy PCG64) and clusters it;
   2. builds the reference's own index on the CPU by importing benchmarks/phase4a_suite.py
      (SharedClusterStorage + TridentV4Index, device="cpu") and records its per-list SQ8 arrays
@@ -30,7 +30,7 @@ from oracle import ref_build, ref_cpu  # noqa: E402
 from trident_b200 import datasets as ds  # noqa: E402
 from trident_b200.clustering import train_clustering  # noqa: E402
 
-REF_ROOT = os.environ.get("TRIDENT_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = ref_build.REF_ROOT
 
 # name -> (base config, overrides, tile size used for the reference build)
 CASES = {

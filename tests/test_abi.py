@@ -47,6 +47,26 @@ def test_version(L):
     assert L.trident_version() == 1
 
 
+def test_noalloc_size_matches_the_header(L):
+    from trident_b200 import _lib
+
+    text = open(os.path.join(ROOT, "include", "trident_b200.h")).read()
+    m = re.search(r"#define TRIDENT_NOALLOC_WORKSPACE_BYTES \((\d+)u \* (\d+)u \* (\d+)u\)", text)
+    assert m, "macro not found"
+    assert _lib.noalloc_workspace_bytes() == int(m.group(1)) * int(m.group(2)) * int(m.group(3))
+
+
+def test_wait_limits_and_status_arguments(L):
+    from trident_b200 import _lib
+
+    assert L.trident_set_wait_limits(0, 0) == 0
+    assert L.trident_set_wait_limits(-1, -1) == 0  # back to the defaults
+    st = ctypes.c_int32(7)
+    assert L.trident_workspace_status(None, None, ctypes.byref(st)) == _lib.TRIDENT_ERR_INVALID
+    assert L.trident_workspace_status(4097 * 256 + 16, None, ctypes.byref(st)) == _lib.TRIDENT_ERR_INVALID
+    assert "aligned" in _lib.last_error()
+
+
 @pytest.mark.parametrize("B,K,nprobe,expect", [
     (1000, 10, 16, 2), (1000, 10, 64, 3), (1, 10, 64, 1), (1, 50, 64, 3), (1000, 10, 1, 0), (100, 10, 2, 2),
 ])
@@ -71,7 +91,7 @@ def _desc(N=100_000, D=128, nlist=256, tile=128):
 
 
 @pytest.mark.parametrize("cfg,B,nprobe,mode", [
-    # W = B * nprobe * (N / nlist) * D against W0 = 9e8
+    # W = B * nprobe * (N / nlist) * D against W0 = 9e8 (phase4a_suite.py:1013-1035, 1079) at C1-C4
     ((100_000, 128, 256), 1000, 16, 10),
     ((1_000_000, 960, 1024), 1000, 64, 2),
     ((10_000_000, 96, 4096), 1, 32, 10),

@@ -1,0 +1,100 @@
+"""Exact probe selection at the configs' list counts (needs a B200), through the C ABI.
+
+probe_select_kernel has three ways to find the nprobe-th approximate coarse value before the exact
+float64 re-check of the boundary:
+  * nlist <= 1024: each thread's keys in registers (c1, c2; covered by test_gpu_search);
+  * nlist <= 8192: the query's row cached in shared memory (c3: nlist 4096);
+  * above that: an upper bound from the coarse GEMM's per-tile row minima, then one pass over the row
+    (c4: nlist 65,536; c5: 262,144), or, when nprobe exceeds the number of 128-list tiles, an exact
+    per-bit search that re-reads the row.
+Each case checks the probe lists and their float64 distances bit for bit against the oracle
+(oracle_probe_select_f64: the nprobe smallest float64 ||q - c||^2, ties to the smaller list id), and
+the search's top-K (ids identical, distances bit-identical) against the oracle's exact IVF-Flat.
+"""
+import numpy as np
+import pytest
+
+from helpers import assert_same_topk, oracle_search
+
+pytestmark = pytest.mark.gpu
+
+
+def _build(cfg, centroid_mode, seed=7):
+    """Rows and queries of cfg's distribution; centroids from a short k-means ("kmeans") or sampled
+    rows ("rows": integer-valued for the int mixtures, so exact float64 ties occur at the boundary)."""
+    import torch
+
+    from trident_b200 import SharedClusterStorage, TridentV4Index, choose_tile, datasets as ds
+    from trident_b200.clustering import assign, train_clustering
+
+    xb = ds.generate_np(cfg, cfg.N, ds.SEED_BASE)
+    xq = ds.generate_np(cfg, cfg.B, ds.SEED_QUERY)
+    if centroid_mode == "kmeans":
+        cent, lids, _, mu, R, _ = train_clustering(xb, cfg.nlist, sample_size=min(cfg.N, 16 * cfg.nlist), niter=4,
+                                                   device="cuda:0")
+    else:
+        rng = np.random.default_rng(seed)
+        cent = np.ascontiguousarray(xb[rng.choice(cfg.N, cfg.nlist, replace=False)])
+        xg = torch.from_numpy(xb).cuda()
+        lids = assign(xg, torch.from_numpy(cent).cuda()).to(torch.int32).cpu().numpy()
+        del xg
+        mu = np.zeros(cfg.D)
+        R = np.linalg.qr(rng.standard_normal((cfg.D, cfg.D)))[0]
+    st = SharedClusterStorage(xb, lids, None, cfg.nlist, device="cuda:0")
+    idx = TridentV4Index(st, cent, mu, R, tile_size=choose_tile(cfg.D), device="cuda:0", max_batch=cfg.B,
+                         max_nprobe=cfg.nprobe)
+    return xb, xq, cent, lids, idx
+
+
+def _coarse_matches_oracle(idx, xq, cent, nprobe):
+    import torch
+
+    from oracle import oracle as O
+
+    cids, d64, _ = idx.coarse(torch.from_numpy(xq).cuda(), nprobe)
+    torch.cuda.synchronize()
+    oc, od = O.probe_select_f64(xq, cent, nprobe)
+    got_c, got_d = cids.cpu().numpy(), d64.cpu().numpy()
+    bad = np.nonzero((got_c != oc).any(axis=1))[0]
+    assert bad.size == 0, f"{bad.size} probe lists differ, first q={bad[0]}"
+    assert np.array_equal(got_d.view(np.uint64), od.view(np.uint64))
+    return oc, od
+
+
+def _search(idx, xq, nprobe, K, mode):
+    import torch
+
+    d, i, _ = idx.search(torch.from_numpy(xq).cuda(), nprobe, mode=mode, k=K)
+    torch.cuda.synchronize()
+    return d.cpu().numpy(), i.cpu().numpy()
+
+
+@pytest.mark.parametrize("cfg_name,over,centroids,modes", [
+    # c3 shape: real-valued rows, 4096 lists, the row cached in shared memory
+    ("c3", dict(N=500_000, nlist=4096, nprobe=128, B=1000, K=10), "kmeans", (2, 10)),
+    # c4 shape: 65,536 lists, the per-tile minimum bound; integer centroids give exact ties
+    ("c4", dict(N=1_000_000, nlist=65_536, nprobe=256, B=1000, K=10), "rows", (2, 10)),
+    # 16,384 lists from k-means (real-valued centroids), the per-tile minimum bound
+    ("c4", dict(N=400_000, nlist=16_384, nprobe=64, B=1000, K=10), "kmeans", (2,)),
+])
+def test_probe_sets_and_topk_at_config_list_counts(cfg_name, over, centroids, modes):
+    from trident_b200 import datasets as ds
+
+    cfg = ds.scaled(ds.CONFIGS[cfg_name], **over)
+    xb, xq, cent, lids, idx = _build(cfg, centroids)
+    oc, _ = _coarse_matches_oracle(idx, xq, cent, cfg.nprobe)
+    od, oi, ocids = oracle_search(xb, lids, cent, xq, cfg.nprobe, cfg.K)
+    assert np.array_equal(ocids, oc)
+    for mode in modes:
+        d, i = _search(idx, xq, cfg.nprobe, cfg.K, mode)
+        assert_same_topk(d, i, od, oi)
+
+
+def test_probe_sets_when_nprobe_exceeds_the_tile_count():
+    """16,384 lists are 128 GEMM tiles; nprobe = 256 cannot be bounded by the per-tile minima, so the
+    exact per-bit search over the row in global memory runs."""
+    from trident_b200 import datasets as ds
+
+    cfg = ds.scaled(ds.CONFIGS["c4"], N=200_000, nlist=16_384, nprobe=256, B=300, K=10)
+    _, xq, cent, _, idx = _build(cfg, "rows")
+    _coarse_matches_oracle(idx, xq, cent, cfg.nprobe)

@@ -21,14 +21,18 @@ from helpers import build_index, load_case
 pytestmark = pytest.mark.gpu
 
 
-def _noalloc(idx, xq_dev, nprobe, K, mode):
+def _noalloc(idx, xq_dev, nprobe, K, mode, out=None):
     import torch
 
     from trident_b200 import _lib
 
     B = int(xq_dev.shape[0])
-    out_d = torch.full((B, K), -7.0, dtype=torch.float32, device=xq_dev.device)
-    out_i = torch.full((B, K), -7, dtype=torch.int64, device=xq_dev.device)
+    if out is None:
+        out = (torch.empty((B, K), dtype=torch.float32, device=xq_dev.device),
+               torch.empty((B, K), dtype=torch.int64, device=xq_dev.device))
+    out_d, out_i = out
+    out_d.fill_(-7.0)
+    out_i.fill_(-7)
     stream = torch.cuda.current_stream(xq_dev.device)
     rc = _lib.lib().trident_search_noalloc(ctypes.byref(idx.desc()), xq_dev.data_ptr(), B, K, nprobe, mode, 0,
                                            out_d.data_ptr(), out_i.data_ptr(), None, stream.cuda_stream)
@@ -53,6 +57,15 @@ def test_noalloc_matches_search_on_two_calls_in_a_row(name):
             d, i = _noalloc(idx, xq, nprobe, K, mode)
             assert np.array_equal(i, ref_i)
             assert np.array_equal(d.view(np.uint32), ref_d.view(np.uint32))
+    # after a first call on this thread and device, further calls take no device memory: the free
+    # memory of the device (cudaMemGetInfo) stays the same across them
+    out = (torch.empty((xq.shape[0], K), dtype=torch.float32, device="cuda"),
+           torch.empty((xq.shape[0], K), dtype=torch.int64, device="cuda"))
+    _noalloc(idx, xq, nprobe, K, 2, out=out)
+    free0 = torch.cuda.mem_get_info()[0]
+    for mode in (2, 10, 2):
+        _noalloc(idx, xq, nprobe, K, mode, out=out)
+    assert torch.cuda.mem_get_info()[0] == free0
     # a different, smaller problem right after: leftovers of the previous call must not matter
     d, i = _noalloc(idx, xq[:5].contiguous(), 2, 3, 2)
     ref_d, ref_i, _ = idx.search(xq[:5].contiguous(), 2, mode=2, k=3)
@@ -70,7 +83,7 @@ def test_noalloc_rejects_a_batch_beyond_its_fixed_workspace():
     idx = build_index(f, device="cuda:0")
     nprobe, K = int(f["nprobe"]), 100
     B = 1
-    while idx.workspace_bytes(B, K, nprobe) <= _lib.NOALLOC_WORKSPACE_BYTES:
+    while idx.workspace_bytes(B, K, nprobe) <= _lib.noalloc_workspace_bytes():
         B *= 2
     xq = torch.zeros((1, idx.D), dtype=torch.float32, device="cuda")  # never read: the size check comes first
     out = torch.empty(1, dtype=torch.float32, device="cuda")

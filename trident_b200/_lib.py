@@ -26,11 +26,21 @@ EXPORTED = (
     "trident_version", "trident_last_error", "trident_index_check", "trident_workspace_size", "trident_p_init",
     "trident_route", "trident_search", "trident_search_profiled", "trident_launch_count", "trident_coarse",
     "trident_merge_shards", "trident_search_noalloc", "trident_search_prep", "trident_search_seed",
-    "trident_search_finish",
+    "trident_search_finish", "trident_workspace_status", "trident_set_wait_limits",
+    "trident_noalloc_workspace_bytes",
 )
 QINFO_LEN = 4
-NOALLOC_WORKSPACE_BYTES = 32 * 1024 * 1024
 PHASES = ("coarse", "pairs", "seed", "scan", "merge")
+
+# device-side status word of a workspace (trident_workspace_status)
+STATUS_OK = 0
+STATUS_LOCK_TIMEOUT = 1
+STATUS_MMA_TIMEOUT = 2
+
+
+def noalloc_workspace_bytes() -> int:
+    """Size of the fixed workspace behind trident_search_noalloc, as compiled into the library."""
+    return int(lib().trident_noalloc_workspace_bytes())
 
 
 class TridentError(RuntimeError):
@@ -97,9 +107,13 @@ def lib():
     L.trident_search_prep.argtypes = [DP, P, i32, i32, P, sz, P, P, P, P]
     L.trident_search_seed.argtypes = [DP, P, i32, i32, i32, i32, i32, P, P, P, P, sz, P, P, P]
     L.trident_search_finish.argtypes = [DP, P, i32, i32, i32, i32, i32, P, P, sz, P, P, P, P]
+    L.trident_workspace_status.argtypes = [P, P, ctypes.POINTER(i32)]
+    L.trident_set_wait_limits.argtypes = [i64, i64]
+    L.trident_noalloc_workspace_bytes.restype = sz
     for name in ("trident_index_check", "trident_workspace_size", "trident_search", "trident_search_profiled",
                  "trident_coarse", "trident_merge_shards", "trident_search_noalloc", "trident_search_prep",
-                 "trident_search_seed", "trident_search_finish"):
+                 "trident_search_seed", "trident_search_finish", "trident_workspace_status",
+                 "trident_set_wait_limits"):
         getattr(L, name).restype = ctypes.c_int
     _LIB = L
     return L
@@ -108,6 +122,11 @@ def lib():
 def check(rc: int) -> None:
     if rc != TRIDENT_OK:
         raise TridentError(rc, lib().trident_last_error().decode(errors="replace"))
+
+
+def set_wait_limits(lock_spins: int = -1, mma_polls: int = -1) -> None:
+    """Process-wide limits of the kernels' bounded waits (-1: the defaults)."""
+    check(lib().trident_set_wait_limits(int(lock_spins), int(mma_polls)))
 
 
 def last_error() -> str:

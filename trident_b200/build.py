@@ -1,7 +1,7 @@
 """Build the trident_b200 CUDA library (sm_100a) in-tree: trident_b200/libtrident_b200.so.
 
-nvcc compiles every csrc/*.cu for `-gencode arch=compute_100a,code=sm_100a` and links one shared
-library exporting the C ABI of include/trident_b200.h. No fast-math: the exact-distance path must
+nvcc compiles every csrc/*.cu for `-gencode arch=compute_100a,code=sm_100a` (one process per source,
+in parallel) and links one shared library exporting the C ABI of include/trident_b200.h. No fast-math: the exact-distance path must
 keep IEEE fmaf/add semantics (the CPU oracle reproduces it bit for bit).
 """
 import glob
@@ -39,13 +39,30 @@ def _stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> str:
+    """Compile each source to an object in parallel (trident_b200/_build/), then link the library."""
     if not force and not _stale():
         return LIB
-    out_tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
-           "-I", INCLUDE, "-I", CSRC, "-o", out_tmp, *sources()]
+    from concurrent.futures import ThreadPoolExecutor
+
+    objdir = os.path.join(PKG, "_build")
+    os.makedirs(objdir, exist_ok=True)
+    flags = [*ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", INCLUDE, "-I", CSRC]
     if ptxas_info:
-        cmd.insert(1, "-Xptxas=-v")
+        flags.insert(0, "-Xptxas=-v")
+
+    def compile_one(src):
+        obj = os.path.join(objdir, os.path.splitext(os.path.basename(src))[0] + ".o")
+        cmd = [nvcc(), *flags, "-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.check_call(cmd)
+        return obj
+
+    srcs = sources()
+    with ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(compile_one, srcs))
+    out_tmp = LIB + ".tmp"
+    cmd = [nvcc(), *ARCH, "-shared", "-o", out_tmp, *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.check_call(cmd)

@@ -11,6 +11,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <string>
 
 #include "tb_internal.h"
@@ -41,6 +42,11 @@ constexpr int kMaxNprobe = 1024;
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Limits of the bounded waits (trident_set_wait_limits); kernels receive them as arguments.
+constexpr uint32_t kDefaultWaitLimit = 1u << 22;
+std::atomic<uint32_t> g_lock_spins{kDefaultWaitLimit};
+std::atomic<uint32_t> g_mma_polls{kDefaultWaitLimit};
+
 }  // namespace
 
 namespace tb {
@@ -48,6 +54,9 @@ namespace tb {
 static_assert(QI_LEN == TRIDENT_QINFO_LEN, "qinfo layout");
 
 int record_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+uint32_t lock_spin_limit() { return g_lock_spins.load(std::memory_order_relaxed); }
+uint32_t mma_wait_limit() { return g_mma_polls.load(std::memory_order_relaxed); }
 
 int num_sms() {
     static int cached[64] = {0};
@@ -73,9 +82,11 @@ size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void*
     const size_t Bs = (size_t)(B > 0 ? B : 1);
     const size_t pairs = Bs * (size_t)nprobe;
     Workspace w;
+    w.ctr = (int32_t*)take(16 * sizeof(int32_t));  // first: the status word's offset is fixed
     w.qrot = (float*)take(Bs * idx.D_pad * sizeof(float));
     w.qinfo = (float*)take(Bs * QI_LEN * sizeof(float));
     w.coarse = (float*)take(Bs * (size_t)idx.nlist * sizeof(float));
+    w.tilemin = (float*)take(Bs * (size_t)((idx.nlist + kCoarseTileN - 1) / kCoarseTileN) * sizeof(float));
     w.probe = (int32_t*)take(pairs * sizeof(int32_t));
     w.cnt = (int32_t*)take(2 * (size_t)idx.nlist * sizeof(int32_t));
     w.off = (int32_t*)take(2 * (size_t)(idx.nlist + 1) * sizeof(int32_t));
@@ -89,7 +100,6 @@ size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void*
     w.tau = (uint32_t*)take(Bs * sizeof(uint32_t));
     w.cand_d = (float*)take(pairs * (size_t)K * sizeof(float));
     w.cand_i = (int32_t*)take(pairs * (size_t)K * sizeof(int32_t));
-    w.ctr = (int32_t*)take(16 * sizeof(int32_t));
     w.bytes = off;
     if (ws) *ws = w;
     return off;
@@ -186,10 +196,11 @@ int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t
     if (!probe_cids) return fail(TRIDENT_ERR_INVALID, "probe_cids is NULL");
     if (B == 0) return TRIDENT_OK;
     cudaStream_t st = (cudaStream_t)stream;
+    TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
     TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, st), "coarse_gemm");
-    TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, probe_cids, probe_d64,
-                               (unsigned long long*)stats, st),
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.tilemin, ws.ctr + kStatusWord, st), "coarse_gemm");
+    TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.tilemin, ws.qinfo, probe_cids, probe_d64,
+                               (unsigned long long*)stats, ws.ctr + kStatusWord, st),
            "probe_select");
     g_launches += 4;
     if (qrot)
@@ -253,8 +264,10 @@ static int stage_coarse(const trident_index* idx, const float* xq, int32_t B, in
     TB_TRY(cudaStreamWaitEvent(ss->s, ss->fork, 0), "fork");
     TB_TRY(launch_rotate_f64(*idx, xq, B, ws.qrot, ss->s), "rotate");
     TB_TRY(cudaEventRecord(ss->join, ss->s), "join");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.ctr + 15, st), "coarse_gemm");
-    TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.qinfo, ws.probe, nullptr, sp, st), "probe_select");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.tilemin, ws.ctr + kStatusWord, st), "coarse_gemm");
+    TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.tilemin, ws.qinfo, ws.probe, nullptr, sp, ws.ctr + kStatusWord,
+                               st),
+           "probe_select");
     g_launches += 4;
     return TRIDENT_OK;
 }
@@ -392,6 +405,26 @@ int trident_search_profiled(const trident_index* idx, const float* xq, int32_t B
 
 int64_t trident_launch_count(void) { return g_launches; }
 
+int trident_workspace_status(const void* workspace, void* stream, int32_t* status) {
+    if (!workspace || !status) return fail(TRIDENT_ERR_INVALID, "workspace / status is NULL");
+    if (((uintptr_t)workspace & 255) != 0) return fail(TRIDENT_ERR_INVALID, "workspace must be 256-byte aligned");
+    cudaStream_t st = (cudaStream_t)stream;
+    int32_t word = 0;
+    // the counter block is the workspace's first region (carve_workspace)
+    const int32_t* src = static_cast<const int32_t*>(workspace) + kStatusWord;
+    TB_TRY(cudaMemcpyAsync(&word, src, sizeof(int32_t), cudaMemcpyDeviceToHost, st), "status copy");
+    TB_TRY(cudaStreamSynchronize(st), "status sync");
+    *status = word;
+    return TRIDENT_OK;
+}
+
+int trident_set_wait_limits(int64_t lock_spins, int64_t mma_polls) {
+    constexpr int64_t kMax = 0x7fffffff;
+    g_lock_spins.store(lock_spins < 0 ? kDefaultWaitLimit : (uint32_t)(lock_spins > kMax ? kMax : lock_spins));
+    g_mma_polls.store(mma_polls < 0 ? kDefaultWaitLimit : (uint32_t)(mma_polls > kMax ? kMax : mma_polls));
+    return TRIDENT_OK;
+}
+
 int trident_search_prep(const trident_index* idx, const float* xq, int32_t B, int32_t nprobe, void* workspace,
                         size_t workspace_bytes, int32_t* probe_out, float* qrot_out, float* qinfo_out, void* stream) {
     Workspace ws;
@@ -432,7 +465,9 @@ int trident_search_seed(const trident_index* idx, const float* xq, int32_t B, in
     TB_TRY(cudaMemcpyAsync(ws.qinfo, qinfo, (size_t)B * TRIDENT_QINFO_LEN * sizeof(float), cudaMemcpyDeviceToDevice,
                            st),
            "qinfo copy");
-    TB_TRY(launch_fill_inf(ws.tau, B, st), "tau init");
+    // tau = +inf; a coarse-stage timeout on any rank reaches this workspace's status word through qinfo
+    TB_TRY(launch_tau_init_import_status(ws.tau, ws.qinfo, B, ws.ctr + kStatusWord, st), "tau init");
+    g_launches += 1;
     const Marker nomark{nullptr, st};
     if (mode != TRIDENT_MODE_CASCADE) {  // CM-FP32 has no seed: empty lists
         TB_TRY(launch_fill_inf(reinterpret_cast<uint32_t*>(seed_d), B * K, st), "seed fill");

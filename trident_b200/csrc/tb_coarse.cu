@@ -192,7 +192,8 @@ constexpr int kSelThreads = 256;
 constexpr int kSelNW = kSelThreads / 32;
 constexpr int kSelCap = 2048;        // sorted best (<= nprobe <= 1024) + one batch of re-check members
 constexpr int kSelSmemKeys = 8192;
-constexpr int kSelRegKeys = 4;      // keys per thread held in registers by the threshold search (nlist <= 1024)   // approximate distances cached in shared memory up to this nlist
+constexpr int kSelRegKeys = 4;      // keys per thread held in registers by the threshold search (nlist <= 1024)
+constexpr int kSelTileKeys = 8;     // per-tile minima per thread (up to 2048 tiles of kCoarseTileN lists)
 
 __device__ void bitonic_sort_kc(unsigned long long* key, int32_t* cid, int P) {
     for (int k = 2; k <= P; k <<= 1) {
@@ -225,6 +226,25 @@ __device__ __forceinline__ int block_sum_sel(int v, int* red) {
     for (int w = 0; w < kSelNW; ++w) s += red[w];
     __syncthreads();
     return s;
+}
+
+// The k-th smallest (1-based) of n keys held R per thread in registers (absent keys: all ones), bit
+// by bit from the top: bit b of the answer is 0 iff at least k keys are <= (the answer so far with
+// bit b = 0 and all lower bits = 1). Padding keys count as <= upper only at upper = 0xFFFFFFFF.
+template <int R>
+__device__ __forceinline__ uint32_t kth_smallest_key(const uint32_t (&kr)[R], int n, int k, int* red) {
+    uint32_t ans = 0;
+    const int pad = R * kSelThreads - n;
+    for (int b = 31; b >= 0; --b) {
+        const uint32_t upper = ans | ((1u << b) - 1u);
+        int cnt = 0;
+#pragma unroll
+        for (int u = 0; u < R; ++u) cnt += kr[u] <= upper;
+        cnt = block_sum_sel(cnt, red);
+        if (upper == 0xFFFFFFFFu) cnt -= pad;
+        if (cnt < k) ans |= (1u << b);
+    }
+    return ans;
 }
 
 // float64 ||q - c||^2 in the oracle's order (oracle_l2_f64): lane l sums d = l, l + 32, ... with
@@ -292,46 +312,61 @@ __device__ __forceinline__ void l2_f64_warp2(const float* __restrict__ qv, const
 }
 
 __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
-    const float* __restrict__ coarse, const float* __restrict__ xq, const float* __restrict__ cent,
-    const float* __restrict__ qinfo, int nlist, int D, int nprobe, float cmax, int32_t* __restrict__ probe,
-    double* __restrict__ probe_d64, unsigned long long* __restrict__ stats) {
+    const float* __restrict__ coarse, const float* __restrict__ tilemin, const float* __restrict__ xq,
+    const float* __restrict__ cent, float* __restrict__ qinfo, int nlist, int D, int nprobe, float cmax,
+    int32_t* __restrict__ probe,
+    double* __restrict__ probe_d64, unsigned long long* __restrict__ stats, const int32_t* __restrict__ err) {
     extern __shared__ float sel_smem[];
     float* qv = sel_smem;                                              // [D]
     uint32_t* skeys = reinterpret_cast<uint32_t*>(sel_smem + ((D + 3) & ~3));  // [nlist] when cached
     __shared__ unsigned long long skey[kSelCap];
     __shared__ int32_t scid[kSelCap];
     __shared__ int red[kSelNW];
-    __shared__ int s_batch;
+    __shared__ int s_batch, s_n;
     const int j = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* row = coarse + (int64_t)j * nlist;
+    // A coarse GEMM that gave up left this row incomplete: no probe list is selected from it. The
+    // status goes into the query's qinfo, which travels with the query in the multi-GPU search.
+    const int32_t status = ld_volatile_i32(err);
+    if (status != 0) {
+        for (int p = tid; p < nprobe; p += blockDim.x) {
+            probe[(int64_t)j * nprobe + p] = -1;
+            if (probe_d64) probe_d64[(int64_t)j * nprobe + p] = __longlong_as_double(0x7ff8000000000000ll);
+        }
+        if (tid == 0) qinfo[(int64_t)j * QI_LEN + QI_PAD] = __int_as_float(status);
+        return;
+    }
     const bool cached = nlist <= kSelSmemKeys;
     for (int d = tid; d < D; d += blockDim.x) qv[d] = xq[(int64_t)j * D + d];
     if (cached)
         for (int c = tid; c < nlist; c += blockDim.x) skeys[c] = float_key(__ldg(row + c));
     __syncthreads();
 
-    // 1) the nprobe-th smallest approximate value, bit by bit from the top: bit b of the answer is
-    //    0 iff at least nprobe keys are <= (answer so far with bit b = 0 and all lower bits = 1)
+    // 1) t >= the nprobe-th smallest approximate value (equal to it except on the tile-minimum path)
     uint32_t ans = 0;
-    if (nlist <= kSelRegKeys * kSelThreads) {  // this thread's keys in registers (absent: all ones)
+    const int ntiles = (nlist + kCoarseTileN - 1) / kCoarseTileN;
+    if (nlist <= kSelRegKeys * kSelThreads) {  // exact, this thread's keys in registers
         uint32_t kr[kSelRegKeys];
 #pragma unroll
         for (int u = 0; u < kSelRegKeys; ++u) {
             const int c = tid + u * kSelThreads;
             kr[u] = c < nlist ? (cached ? skeys[c] : float_key(__ldg(row + c))) : 0xFFFFFFFFu;
         }
-        const int pad = kSelRegKeys * kSelThreads - nlist;  // padding keys count as <= upper only at 0xFFFFFFFF
-        for (int b = 31; b >= 0; --b) {
-            const uint32_t upper = ans | ((1u << b) - 1u);
-            int cnt = 0;
+        ans = kth_smallest_key<kSelRegKeys>(kr, nlist, nprobe, red);
+    } else if (!cached && tilemin && nprobe <= ntiles && ntiles <= kSelTileKeys * kSelThreads) {
+        // An upper bound from the GEMM's per-tile minima: the nprobe smallest of them are nprobe
+        // distinct entries of the row, so the row's nprobe-th smallest value is <= their largest.
+        // The member pass below then reads the row once instead of once per bit.
+        uint32_t kr[kSelTileKeys];
+        const float* tm = tilemin + (int64_t)j * ntiles;
 #pragma unroll
-            for (int u = 0; u < kSelRegKeys; ++u) cnt += kr[u] <= upper;
-            cnt = block_sum_sel(cnt, red);
-            if (upper == 0xFFFFFFFFu) cnt -= pad;
-            if (cnt < nprobe) ans |= (1u << b);
+        for (int u = 0; u < kSelTileKeys; ++u) {
+            const int c = tid + u * kSelThreads;
+            kr[u] = c < ntiles ? float_key(__ldg(tm + c)) : 0xFFFFFFFFu;
         }
-    } else {
+        ans = kth_smallest_key<kSelTileKeys>(kr, ntiles, nprobe, red);
+    } else {  // exact, keys re-read per bit (shared memory when cached)
         for (int b = 31; b >= 0; --b) {
             const uint32_t upper = ans | ((1u << b) - 1u);
             int cnt = 0;
@@ -387,7 +422,32 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
         if (tid == 0) s_batch = 0;
         __syncthreads();
     };
-    for (int cs = 0; cs < nlist; cs += blockDim.x) {
+    // One pass with warp-aggregated appends and no CTA barrier; if the members overflow the buffer,
+    // the chunked pass below takes them in batches instead.
+    if (tid == 0) s_n = 0;
+    __syncthreads();
+    for (int c0 = warp * 32; c0 < nlist; c0 += kSelThreads) {  // warp-uniform trip count
+        const int c = c0 + lane;
+        const bool mem = (c < nlist) && ((cached ? key_float(skeys[c]) : __ldg(row + c)) <= thr);
+        const unsigned m = __ballot_sync(TB_FULL, mem);
+        if (m) {
+            const int leader = __ffs(m) - 1;
+            int pos = 0;
+            if (lane == leader) pos = atomicAdd(&s_n, __popc(m));
+            pos = __shfl_sync(TB_FULL, pos, leader) + __popc(m & ((1u << lane) - 1u));
+            if (mem && pos < kSelCap) scid[pos] = c;
+        }
+    }
+    __syncthreads();
+    const int n_fast = s_n;
+    if (n_fast <= kSelCap) {
+        members = n_fast;
+        if (n_fast > 0) {
+            batch = n_fast;
+            process_batch();
+        }
+    }
+    for (int cs = 0; n_fast > kSelCap && cs < nlist; cs += blockDim.x) {
         const int c = cs + tid;
         const bool mem = (c < nlist) && ((cached ? key_float(skeys[c]) : __ldg(row + c)) <= thr);
         const int chunk = __syncthreads_count(mem);
@@ -418,14 +478,14 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
 }
 
 cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B, int nprobe, const float* coarse,
-                                const float* qinfo, int32_t* probe, double* probe_d64, unsigned long long* stats,
-                                cudaStream_t st) {
+                                const float* tilemin, float* qinfo, int32_t* probe, double* probe_d64,
+                                unsigned long long* stats, const int32_t* err, cudaStream_t st) {
     size_t smem = (size_t)((idx.D + 3) & ~3) * sizeof(float);
     if (idx.nlist <= kSelSmemKeys) smem += (size_t)idx.nlist * sizeof(uint32_t);
     cudaError_t e = cudaFuncSetAttribute(probe_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    probe_select_kernel<<<B, kSelThreads, smem, st>>>(coarse, xq, idx.centroids, qinfo, idx.nlist, idx.D, nprobe,
-                                                      idx.centroid_norm_max, probe, probe_d64, stats);
+    probe_select_kernel<<<B, kSelThreads, smem, st>>>(coarse, tilemin, xq, idx.centroids, qinfo, idx.nlist, idx.D, nprobe,
+                                                      idx.centroid_norm_max, probe, probe_d64, stats, err);
     return cudaGetLastError();
 }
 

@@ -31,7 +31,7 @@
 namespace tb {
 
 constexpr int kCM = 128;  // queries per tile (UMMA M)
-constexpr int kCN = 128;  // lists per tile (UMMA N)
+constexpr int kCN = kCoarseTileN;  // lists per tile (UMMA N)
 constexpr int kCK = 32;   // K per stage: 4 UMMA k-steps of 8 TF32 values
 constexpr int kCThreads = 128;
 constexpr int kCChunks = kCK / 4;                // 16-byte K chunks per stage
@@ -41,7 +41,7 @@ constexpr int kCStageBytes = 2 * kCAbytes + 2 * kCBbytes;
 // two stages + alignment slack + a 32 KB guard: a descriptor whose two strides were read the other
 // way round would still address only this CTA's shared memory
 constexpr int kCSmem = 2 * kCStageBytes + 32768 + 1024;
-constexpr uint32_t kCWaitTries = 1u << 22;       // bounded mbarrier polling
+constexpr uint32_t kCWaitTries = 1u << 22;       // bounded mbarrier polling while draining after a timeout
 constexpr uint32_t kCTmemCols = kCN;  // one float32 column per list of the tile (a power of 2 >= 32)
 
 // Instruction descriptor: D = F32 (bits 4-5 = 1), A = B = TF32 (bits 7-9, 10-12 = 2), both
@@ -86,9 +86,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait for the phase with the given parity; false if it did not complete in time.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kCWaitTries; ++i)
+// Bounded wait for the phase with the given parity (at most `polls` polls); false if it did not
+// complete in time.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t polls) {
+    for (uint32_t i = 0; i < polls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
 }
@@ -139,7 +140,9 @@ __global__ void __launch_bounds__(kCThreads, 1) coarse_mma_kernel(const float* _
                                                                   const float* __restrict__ cent,
                                                                   const float* __restrict__ cn, int B, int nlist,
                                                                   int D, float* __restrict__ out,
-                                                                  int32_t* __restrict__ err) {
+                                                                  float* __restrict__ tilemin,
+                                                                  int32_t* __restrict__ err, uint32_t polls,
+                                                                  int vec_out) {
     extern __shared__ unsigned char c_smem_raw[];
     __shared__ __align__(8) uint64_t s_bar[2];
     __shared__ uint32_t s_tmem;
@@ -175,7 +178,7 @@ __global__ void __launch_bounds__(kCThreads, 1) coarse_mma_kernel(const float* _
         float4 va[kCChunks], vb[kCChunks];
         load_split_row<VEC>(xq, B, D, m0 + tid, kt * kCK, va);
         if (tid < kCN) load_split_row<VEC>(cent, nlist, D, n0 + tid, kt * kCK, vb);
-        if (kt >= 2 && !mbar_wait(&s_bar[s], (uint32_t)((kt - 2) >> 1) & 1u)) ok = false;  // stage free?
+        if (kt >= 2 && !mbar_wait(&s_bar[s], (uint32_t)((kt - 2) >> 1) & 1u, polls)) ok = false;  // stage free?
         if (!__syncthreads_and(ok)) {
             ok = false;
             break;
@@ -204,14 +207,16 @@ __global__ void __launch_bounds__(kCThreads, 1) coarse_mma_kernel(const float* _
     }
     // the last commit covers every MMA issued before it
     const int last = committed - 1;
-    if (ok && last >= 0 && !mbar_wait(&s_bar[last & 1], (uint32_t)(last >> 1) & 1u)) ok = false;
+    if (ok && last >= 0 && !mbar_wait(&s_bar[last & 1], (uint32_t)(last >> 1) & 1u, polls)) ok = false;
     ok = __syncthreads_and(ok) != 0;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
 
     if (ok) {
-        // epilogue: warp w reads tensor-memory lanes 32w..32w+31 (rows), 16 columns per load
+        // epilogue: warp w reads tensor-memory lanes 32w..32w+31 (rows), 16 columns per load; each
+        // thread also keeps its row's minimum over the tile's lists (the selection's upper bound)
         const int row = m0 + warp * 32 + lane;
         const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
+        float rmin = kInf;
         for (int c0 = 0; c0 < kCN; c0 += 16) {
             uint32_t r[16];
             asm volatile(
@@ -223,17 +228,39 @@ __global__ void __launch_bounds__(kCThreads, 1) coarse_mma_kernel(const float* _
                 : "r"(taddr + (uint32_t)c0));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             if (row < B) {
+                const int col0 = n0 + c0;
+                float* dst = out + (int64_t)row * nlist + col0;
+                if (vec_out && col0 + 16 <= nlist) {
+                    const float4* cn4 = reinterpret_cast<const float4*>(cn + col0);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int col = n0 + c0 + j;
-                    if (col < nlist) out[(int64_t)row * nlist + col] = __ldg(cn + col) - 2.0f * __uint_as_float(r[j]);
+                    for (int v = 0; v < 4; ++v) {
+                        const float4 c = __ldg(cn4 + v);
+                        float4 o;
+                        o.x = c.x - 2.0f * __uint_as_float(r[4 * v + 0]);
+                        o.y = c.y - 2.0f * __uint_as_float(r[4 * v + 1]);
+                        o.z = c.z - 2.0f * __uint_as_float(r[4 * v + 2]);
+                        o.w = c.w - 2.0f * __uint_as_float(r[4 * v + 3]);
+                        rmin = fminf(rmin, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
+                        reinterpret_cast<float4*>(dst)[v] = o;
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        if (col0 + j < nlist) {
+                            const float o = __ldg(cn + col0 + j) - 2.0f * __uint_as_float(r[j]);
+                            rmin = fminf(rmin, o);
+                            dst[j] = o;
+                        }
+                    }
                 }
             }
         }
+        if (tilemin && row < B) tilemin[(int64_t)row * gridDim.x + blockIdx.x] = rmin;
     } else {
-        if (tid == 0) atomicExch(err, 2);
-        // let any MMA still in flight finish (bounded) before the tensor memory is released
-        if (last >= 0) mbar_wait(&s_bar[last & 1], (uint32_t)(last >> 1) & 1u);
+        if (tid == 0) atomicOr(err, TRIDENT_STATUS_MMA_TIMEOUT);
+        // let any MMA still in flight finish (bounded, at the full default limit whatever `polls`
+        // is) before the tensor memory is released
+        if (last >= 0) mbar_wait(&s_bar[last & 1], (uint32_t)(last >> 1) & 1u, kCWaitTries);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -243,22 +270,25 @@ __global__ void __launch_bounds__(kCThreads, 1) coarse_mma_kernel(const float* _
     }
 }
 
-cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, int32_t* err,
-                               cudaStream_t st) {
+cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, float* tilemin,
+                               int32_t* err, cudaStream_t st) {
     if (B <= 0) return cudaSuccess;
     const bool vec = (idx.D % 4) == 0 && (((uintptr_t)xq | (uintptr_t)idx.centroids) & 15) == 0;
     dim3 grid((idx.nlist + kCN - 1) / kCN, (B + kCM - 1) / kCM);
+    // 16-byte epilogue stores and norm loads: rows start 16-byte aligned (the workspace region is
+    // 256-byte aligned) when nlist % 4 == 0, and the norms must be 16-byte aligned too
+    const int vec_out = (idx.nlist % 4) == 0 && (((uintptr_t)coarse | (uintptr_t)idx.centroid_norm_sq) & 15) == 0;
     cudaError_t e;
     if (vec) {
         e = cudaFuncSetAttribute(coarse_mma_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kCSmem);
         if (e != cudaSuccess) return e;
         coarse_mma_kernel<true><<<grid, kCThreads, kCSmem, st>>>(xq, idx.centroids, idx.centroid_norm_sq, B,
-                                                                 idx.nlist, idx.D, coarse, err);
+                                                                 idx.nlist, idx.D, coarse, tilemin, err, mma_wait_limit(), vec_out);
     } else {
         e = cudaFuncSetAttribute(coarse_mma_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kCSmem);
         if (e != cudaSuccess) return e;
         coarse_mma_kernel<false><<<grid, kCThreads, kCSmem, st>>>(xq, idx.centroids, idx.centroid_norm_sq, B,
-                                                                  idx.nlist, idx.D, coarse, err);
+                                                                  idx.nlist, idx.D, coarse, tilemin, err, mma_wait_limit(), vec_out);
     }
     return cudaGetLastError();
 }

@@ -9,14 +9,22 @@
 
 namespace tb {
 
-// Per-query side information written by the rotation kernel.
+// Per-query side information written by the rotation kernel. QI_PAD carries the int bits of the
+// coarse stage's status (0 = ok) for that query.
 enum QInfo { QI_QNORM = 0, QI_SIGMA = 1, QI_CNORM = 2, QI_PAD = 3, QI_LEN = 4 };
 
-// Workspace carve-up for one call (B, K, nprobe); every region is 256-byte aligned.
+// Word of the counter block that holds the search's device-side status (TRIDENT_STATUS_*).
+constexpr int kStatusWord = 15;
+// Lists per tile of the coarse GEMM (and per entry of its per-tile row minima).
+constexpr int kCoarseTileN = 128;
+
+// Workspace carve-up for one call (B, K, nprobe); every region is 256-byte aligned. The counter
+// block comes first, so the status word sits at the same offset whatever B, K and nprobe are.
 struct Workspace {
     float* qrot;        // [B, D_pad]
     float* qinfo;       // [B, QI_LEN]
     float* coarse;      // [B, nlist] approximate ||c||^2 - 2 q.c
+    float* tilemin;     // [B, ceil(nlist / kCoarseTileN)] minimum of each row over each GEMM tile
     int32_t* probe;     // [B, nprobe]
     int32_t* cnt;       // [2, nlist]
     int32_t* off;       // [2, nlist + 1]
@@ -30,9 +38,13 @@ struct Workspace {
     uint32_t* tau;      // [B] float bits of each query's current K-th distance
     float* cand_d;      // [B, nprobe, K]
     int32_t* cand_i;    // [B, nprobe, K]
-    int32_t* ctr;       // [16] item counts and work counters
+    int32_t* ctr;       // [16] item counts and work counters; ctr[kStatusWord] = status
     size_t bytes;
 };
+
+// Process-wide limits of the bounded waits (trident_set_wait_limits).
+uint32_t lock_spin_limit();   // per-query insertion lock of the scan
+uint32_t mma_wait_limit();    // tensor-core completion (mbarrier) polls of the coarse GEMM
 
 size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void* base, Workspace* ws);
 
@@ -44,12 +56,18 @@ cudaError_t launch_query_norms(const trident_index& idx, const float* xq, int B,
 cudaError_t launch_rotate_f64(const trident_index& idx, const float* xq, int B, float* qrot, cudaStream_t st);
 cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
                           uint32_t* tau, cudaStream_t st);
-// tcgen05 3xTF32 GEMM (tb_coarse_mma.cu); sets *err = 2 if a bounded wait gave up.
-cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, int32_t* err,
-                               cudaStream_t st);
+// tcgen05 3xTF32 GEMM (tb_coarse_mma.cu); sets *err = TRIDENT_STATUS_MMA_TIMEOUT if a bounded wait
+// gave up.
+// tilemin (optional, [B, ceil(nlist / kCoarseTileN)]) receives each row's minimum over each tile.
+cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, float* tilemin,
+                               int32_t* err, cudaStream_t st);
+// Exact probe lists. A nonzero *err (the GEMM gave up) marks every probe list -1 (and probe_d64 NaN)
+// and is copied into each query's qinfo[QI_PAD], which travels with the query to other GPUs.
+// tilemin (optional) lets selection above 8192 lists bound the nprobe-th value without re-reading
+// the row per bit.
 cudaError_t launch_probe_select(const trident_index& idx, const float* xq, int B, int nprobe, const float* coarse,
-                                const float* qinfo, int32_t* probe, double* probe_d64,
-                                unsigned long long* stats, cudaStream_t st);
+                                const float* tilemin, float* qinfo, int32_t* probe, double* probe_d64,
+                                unsigned long long* stats, const int32_t* err, cudaStream_t st);
 
 // Pair lists and work items (tb_pairs.cu).
 cudaError_t launch_pairs(const trident_index& idx, const int32_t* probe, int B, int nprobe, int p_init, int G, int K,
@@ -61,6 +79,9 @@ cudaError_t launch_item_order(const trident_index& idx, int max_items, const Wor
 
 // tau[0..n) = +inf (float bits), tb_seed.cu.
 cudaError_t launch_fill_inf(uint32_t* tau, int n, cudaStream_t st);
+// tau[0..B) = +inf, and the status that a query's coarse stage left in qinfo[QI_PAD] (possibly on
+// another GPU) is or-ed into *err.
+cudaError_t launch_tau_init_import_status(uint32_t* tau, const float* qinfo, int B, int32_t* err, cudaStream_t st);
 
 // Query-major threshold seeding (tb_seed.cu): rank the rows of each query's p_seed nearest lists by
 // a partial SQ8 distance, refine the best exactly (or bound them from above with ub) and store the

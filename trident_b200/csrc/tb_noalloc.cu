@@ -15,7 +15,10 @@
 // value before reading it, so the contents left by the previous call do no harm.
 //
 // The first call on each device looks up the array's device address (cudaGetSymbolAddress, with
-// that device current) and caches it; make that first call before capturing any stream.
+// that device current) and caches it. Like trident_search, the first search from each host thread on
+// each device also creates the library's side stream and its four events (which are not device
+// memory allocations, but are not allowed during stream capture either): make that first call
+// before capturing any stream.
 #include <cuda_runtime.h>
 #include <stdio.h>
 
@@ -76,3 +79,5 @@ extern "C" int trident_search_noalloc(const trident_index* idx, const float* xq,
     return trident_search(idx, xq, B, K, nprobe, mode, ub_seed, ws, (size_t)TRIDENT_NOALLOC_WORKSPACE_BYTES, out_d,
                           out_i, stats, stream);
 }
+
+extern "C" size_t trident_noalloc_workspace_bytes(void) { return (size_t)TRIDENT_NOALLOC_WORKSPACE_BYTES; }

@@ -41,7 +41,8 @@ struct ScanArgs {
     float* cand_d;
     int32_t* cand_i;
     unsigned long long* stats;
-    int32_t* err;  // set to 1 if a per-query lock wait gave up (results then marked invalid)
+    int32_t* err;  // status word: TRIDENT_STATUS_LOCK_TIMEOUT if a per-query lock wait gave up
+    uint32_t lock_spins;  // limit of that wait (tries)
     int D, D_pad, nb, K, nprobe, G;
     int seed_rows;  // best-ranked rows refined first for queries without a finite threshold (0: off)
     float rho;
@@ -162,7 +163,6 @@ constexpr float kU32 = 5.9604644775390625e-08f;  // 2^-24
 constexpr int kSCS = 196;  // floats per query of scaled block-0/1 intervals: 16 groups x 12, +4 (banks)
 constexpr int kWB = 64;    // per-warp block-1 batch capacity
 constexpr int kWQ = 64;    // per-warp deep-queue capacity (<= 31 waiting + 32 new entries)
-constexpr int kLockSpins = 1 << 22;  // bounded wait for a per-query insertion lock
 
 // One 4-dim group of the scaled bound: two packed FFMA2 for u' = c * delta' + base', four
 // saturating |u'| - eps', two packed FFMA2 into the running pair of partial sums.
@@ -548,14 +548,14 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                 const int32_t id = __ldg(a.oid + r0 + r);
                 int got = 0;
                 if (lane == 0) {
-                    for (int spin = 0; spin < kLockSpins; ++spin) {
+                    for (uint32_t spin = 0; spin < a.lock_spins; ++spin) {
                         if (atomicCAS(&s_lock[j], 0, 1) == 0) { got = 1; break; }
                         __nanosleep(64);
                     }
                 }
                 got = __shfl_sync(TB_FULL, got, 0);
                 if (!got) {  // never expected: the holder is a warp of this CTA doing one insertion
-                    if (lane == 0) atomicExch(a.err, 1);
+                    if (lane == 0) atomicOr(a.err, TRIDENT_STATUS_LOCK_TIMEOUT);
                     return;
                 }
                 __threadfence_block();
@@ -942,6 +942,7 @@ __global__ void __launch_bounds__(256) merge_shards_kernel(const float* __restri
     list_init<KM>(ld, li, lane);
     __syncwarp();
     const int n = R * K;
+    bool bad = false;  // some shard marked this query: a bounded wait gave up there
     for (int k0 = 0; k0 < n; k0 += 32) {
         const int k = k0 + lane;
         float d = kInf;
@@ -951,12 +952,14 @@ __global__ void __launch_bounds__(256) merge_shards_kernel(const float* __restri
             d = d_in[((int64_t)r * B + q) * K + kk];
             id = i_in[((int64_t)r * B + q) * K + kk];
         }
+        bad |= id == -2;
         list_offer<KM>(ld, li, K, id >= 0, d, (int32_t)id, lane);
     }
+    bad = __any_sync(TB_FULL, bad);
     __syncwarp();
     for (int k = lane; k < K; k += 32) {
-        out_d[(int64_t)q * K + k] = ld[k];
-        out_i[(int64_t)q * K + k] = (int64_t)li[k];
+        out_d[(int64_t)q * K + k] = bad ? __int_as_float(0x7fc00000) : ld[k];
+        out_i[(int64_t)q * K + k] = bad ? (int64_t)-2 : (int64_t)li[k];
     }
 }
 
@@ -1046,7 +1049,8 @@ cudaError_t launch_scan(const trident_index& idx, const float* xq, const Workspa
     a.cand_d = ws.cand_d;
     a.cand_i = ws.cand_i;
     a.stats = stats;
-    a.err = ws.ctr + 15;
+    a.err = ws.ctr + kStatusWord;
+    a.lock_spins = lock_spin_limit();
     a.D = idx.D;
     a.D_pad = idx.D_pad;
     a.nb = idx.num_blocks;
@@ -1070,10 +1074,10 @@ cudaError_t launch_merge(const Workspace& ws, int B, int K, int nprobe, int p_lo
     const int grid = (B + 7) / 8;
     if (K <= 32)
         merge_kernel<32><<<grid, 256, 0, st>>>(ws.cand_d, ws.cand_i, B, K, nprobe, p_lo, p_hi, tau_out, out_d, out_i,
-                                                ws.ctr + 15);
+                                                ws.ctr + kStatusWord);
     else
         merge_kernel<128><<<grid, 256, 0, st>>>(ws.cand_d, ws.cand_i, B, K, nprobe, p_lo, p_hi, tau_out, out_d, out_i,
-                                                 ws.ctr + 15);
+                                                 ws.ctr + kStatusWord);
     return cudaGetLastError();
 }
 

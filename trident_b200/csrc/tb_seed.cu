@@ -338,6 +338,23 @@ cudaError_t launch_fill_inf(uint32_t* tau, int n, cudaStream_t st) {
     return cudaGetLastError();
 }
 
+// tau = +inf for every query; the coarse-stage status each query carries in qinfo[QI_PAD] (written
+// by probe selection, possibly on another GPU) is or-ed into the workspace's status word.
+__global__ void tau_init_import_status_kernel(uint32_t* __restrict__ tau, const float* __restrict__ qinfo, int B,
+                                              int32_t* __restrict__ err) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < B; i += gridDim.x * blockDim.x) {
+        tau[i] = __float_as_uint(kInf);
+        const int32_t s = __float_as_int(qinfo[(int64_t)i * QI_LEN + QI_PAD]);
+        if (s != 0) atomicOr(err, s);
+    }
+}
+
+cudaError_t launch_tau_init_import_status(uint32_t* tau, const float* qinfo, int B, int32_t* err, cudaStream_t st) {
+    if (B <= 0) return cudaSuccess;
+    tau_init_import_status_kernel<<<(B + 255) / 256 < 1024 ? (B + 255) / 256 : 1024, 256, 0, st>>>(tau, qinfo, B, err);
+    return cudaGetLastError();
+}
+
 int seed_rows_for(int K) { return 32 * ((K + 31) / 32) < 64 ? 64 : 32 * ((K + 31) / 32); }
 
 int seed_lists_for(int B, int K, int nprobe) {

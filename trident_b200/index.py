@@ -275,6 +275,20 @@ class TridentV4Index:
             self._out[K] = buf
         return buf[0][:B], buf[1][:B]
 
+    def status(self) -> int:
+        """Device-side status word of this index's workspace after its last search (waits for the
+        current stream): 0, or an OR of _lib.STATUS_LOCK_TIMEOUT / _lib.STATUS_MMA_TIMEOUT when a
+        bounded wait gave up and the results were marked (NaN, -2)."""
+        import ctypes
+
+        torch = _torch()
+        if self._ws is None:
+            return 0
+        st = ctypes.c_int32(0)
+        _lib.check(_lib.lib().trident_workspace_status(_ptr(self._ws), torch.cuda.current_stream(self.dev).cuda_stream,
+                                                       ctypes.byref(st)))
+        return int(st.value)
+
     def route(self, B: int, nprobe: int, w0: float = 9.0e8) -> int:
         return int(_lib.lib().trident_route(self.desc(), int(B), int(nprobe), float(w0)))
 
