@@ -193,14 +193,12 @@ class ClockSampler:
 
 
 # ----------------------------------------------------------------------------------------------
-def make_workload(args, d: Dist):
-    """Generate the config's rows/queries, cluster (rank 0, broadcast) and build this rank's shard."""
-    import numpy as np
-    import torch
+STRONG = ("c4", "c5")  # configs whose query count is the job's total (split across ranks)
+CPU_SAMPLE_CAP = {"c4": 1000, "c5": 100}  # CPU-baseline query prefix
 
-    from trident_b200 import SharedClusterStorage, TridentV4Index, choose_tile, datasets as ds
-    from trident_b200.clustering import train_clustering
-    from trident_b200.shard import partition_lists
+
+def workload_config(args):
+    from trident_b200 import datasets as ds
 
     cfg = ds.CONFIGS[args.config]
     over = {}
@@ -214,53 +212,115 @@ def make_workload(args, d: Dist):
         over["N"] = args.n
     if over:
         cfg = ds.scaled(cfg, **over)
-    t0 = time.perf_counter()
+    return cfg
+
+
+def make_clustering(args, d: Dist, cfg):
+    """Rows generated on the GPU (every rank the same rows), clustered on rank 0 and broadcast.
+    Returns (xb on the device, own queries, c_np, l_np, mu_np, R_np, strong)."""
+    import numpy as np
+    import torch
+
+    from trident_b200 import datasets as ds
+    from trident_b200.clustering import train_clustering
+
+    strong = cfg.name.split("_")[0] in STRONG
     xb = ds.generate_torch(cfg, cfg.N, ds.SEED_BASE, device=d.dev)
-    # each rank brings its own B queries (weak scaling); rank r holds rows [r B, (r + 1) B)
-    xq = ds.generate_np(cfg, cfg.B * d.world, ds.SEED_QUERY)[d.rank * cfg.B:(d.rank + 1) * cfg.B]
+    if strong:  # the config's B queries are the job's; rank r takes its slice
+        if cfg.B % d.world:
+            raise SystemExit(f"B={cfg.B} does not split over {d.world} ranks")
+        per = cfg.B // d.world
+        xq = ds.generate_np(cfg, cfg.B, ds.SEED_QUERY)[d.rank * per:(d.rank + 1) * per]
+    else:  # each rank brings its own B queries; rank r holds rows [r B, (r + 1) B)
+        xq = ds.generate_np(cfg, cfg.B * d.world, ds.SEED_QUERY)[d.rank * cfg.B:(d.rank + 1) * cfg.B]
     xq = np.ascontiguousarray(xq)
     cent = torch.empty((cfg.nlist, cfg.D), dtype=torch.float32, device=d.dev)
     lids = torch.empty(cfg.N, dtype=torch.int32, device=d.dev)
     mu = torch.empty(cfg.D, dtype=torch.float64, device=d.dev)
     R = torch.empty((cfg.D, cfg.D), dtype=torch.float64, device=d.dev)
     if d.rank == 0:
-        c_np, l_np, _, mu_np, R_np, train_s = train_clustering(xb, cfg.nlist, sample_size=cfg.sample_size(),
-                                                               device=d.dev)
+        t0 = time.perf_counter()
+        c_np, l_np, _, mu_np, R_np, _ = train_clustering(xb, cfg.nlist, sample_size=cfg.sample_size(), device=d.dev)
         cent.copy_(torch.from_numpy(c_np))
         lids.copy_(torch.from_numpy(l_np))
         mu.copy_(torch.from_numpy(mu_np))
         R.copy_(torch.from_numpy(R_np))
+        log(f"[rank 0] clustering of {cfg.N} rows into {cfg.nlist} lists: {time.perf_counter() - t0:.1f}s")
     for t in (cent, lids, mu, R):
         d.bcast(t)
     torch.cuda.synchronize()
-    c_np, l_np, mu_np, R_np = cent.cpu().numpy(), lids.cpu().numpy(), mu.cpu().numpy(), R.cpu().numpy()
+    return xb, xq, lids, cent.cpu().numpy(), lids.cpu().numpy(), mu.cpu().numpy(), R.cpu().numpy(), strong
+
+
+def make_workload(args, d: Dist):
+    """Generate the config's rows/queries, cluster (rank 0, broadcast) and build this rank's shard.
+    The full row array is dropped once the shard's storage is built."""
+    import numpy as np
+    import torch
+
+    from trident_b200 import SharedClusterStorage, TridentV4Index, choose_tile
+    from trident_b200.shard import partition_lists
+
+    cfg = workload_config(args)
+    t0 = time.perf_counter()
+    xb, xq, lids, c_np, l_np, mu_np, R_np, strong = make_clustering(args, d, cfg)
     if d.world > 1:
         counts = np.bincount(l_np, minlength=cfg.nlist)
         owner = torch.from_numpy(partition_lists(counts, d.world)).to(d.dev)
         rows = torch.nonzero(owner[lids.long()] == d.rank).flatten()
         st = SharedClusterStorage(xb[rows], lids[rows], None, cfg.nlist, device=d.dev, host_rows=args.ooc)
         st.orig_ids_sorted = rows.to(torch.int32)[st.orig_ids_sorted.long()].contiguous()
+        del rows, owner
     else:
         st = SharedClusterStorage(xb, lids, None, cfg.nlist, device=d.dev, host_rows=args.ooc)
-    idx = TridentV4Index(st, c_np, mu_np, R_np, tile_size=choose_tile(cfg.D), device=d.dev, max_batch=cfg.B,
+    del xb, lids
+    torch.cuda.empty_cache()
+    idx = TridentV4Index(st, c_np, mu_np, R_np, tile_size=choose_tile(cfg.D), device=d.dev,
+                         max_batch=max(1, xq.shape[0]) * d.world,
                          max_nprobe=cfg.nprobe, max_k=cfg.K)
     torch.cuda.synchronize()
     log(f"[rank {d.rank}] built {cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} shard rows={st.N} "
-        f"in {time.perf_counter() - t0:.1f}s (index build {idx.build_s:.1f}s)")
-    return cfg, xb, xq, c_np, l_np, idx
+        f"in {time.perf_counter() - t0:.1f}s (index build {idx.build_s:.1f}s, peak device memory "
+        f"{torch.cuda.max_memory_allocated(d.dev) / 1e9:.1f} GB)")
+    return cfg, xq, c_np, l_np, idx, strong
 
 
-def host_storage(xb, l_np, nlist):
-    """Host copies of the full (unsharded) list-sorted storage for the CPU oracle / baseline."""
+def host_storage(cfg, l_np, lists, device):
+    """Host copies of the rows of `lists` in the index's order (list-major, original ids ascending
+    within a list), regenerated on `device` chunk by chunk from the seeded generator, so that no
+    process keeps the whole row array. Other lists are empty in the returned offsets, so a search
+    whose probes all lie in `lists` sees exactly the full dataset's lists.
+    Returns (xs [n, D] float32 torch CPU tensor, perm [n] int32 original ids, off [nlist + 1] int64)."""
     import numpy as np
     import torch
 
-    perm = np.argsort(l_np, kind="stable").astype(np.int32)
-    counts = np.bincount(l_np, minlength=nlist)
-    off = np.zeros(nlist + 1, np.int64)
+    from trident_b200 import datasets as ds
+
+    need = np.zeros(cfg.nlist, bool)
+    need[np.asarray(lists, np.int64)] = True
+    counts = np.bincount(l_np, minlength=cfg.nlist)
+    counts[~need] = 0
+    off = np.zeros(cfg.nlist + 1, np.int64)
     off[1:] = np.cumsum(counts)
-    xs = torch.empty((xb.shape[0], xb.shape[1]), dtype=torch.float32, pin_memory=True)
-    xs.copy_(xb[torch.from_numpy(perm).to(xb.device).long()])
+    sel = np.nonzero(need[l_np])[0]                       # original ids, ascending
+    order = np.argsort(l_np[sel], kind="stable")          # list-major
+    perm = sel[order].astype(np.int32)
+    dest = np.empty(len(sel), np.int64)
+    dest[order] = np.arange(len(sel))                     # destination row of sel[k]
+    # the rows are put in order on the device (one scatter per generated chunk), then copied to
+    # pageable host memory in one piece
+    xs_dev = torch.empty((len(sel), cfg.D), dtype=torch.float32, device=device)
+    sel_dev = torch.from_numpy(sel).to(device)
+    dest_dev = torch.from_numpy(dest).to(device)
+    for s, e, x in ds.iter_torch_chunks(cfg, cfg.N, ds.SEED_BASE, device=device):
+        a, b = (int(v) for v in np.searchsorted(sel, [s, e]))
+        if b > a:
+            xs_dev.index_copy_(0, dest_dev[a:b], x[sel_dev[a:b] - s])
+    del sel_dev, dest_dev
+    xs = xs_dev.cpu()
+    del xs_dev
+    if str(device).startswith("cuda"):
+        torch.cuda.empty_cache()
     return xs, perm, off
 
 
@@ -293,24 +353,35 @@ def host_threads():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(args, cfg, xq, c_np, xs, perm, off):
+def data_desc(cfg) -> str:
+    kind = {"int_mixture": f"SIFT-shaped integer rows in [0, 255] ({cfg.n_comp}-component mixture, sigma={cfg.sigma})",
+            "decay": "GIST1M-shaped decay-spectrum rows",
+            "norm_mixture": f"Deep-shaped L2-normalised rows ({cfg.n_comp}-component mixture, sigma={cfg.sigma})"}
+    return f"synthetic (seeded {kind.get(cfg.kind, cfg.kind)}, generated on the GPU)"
+
+
+def cpu_baseline(args, cfg, xq, c_np, xs, perm, off, n_max):
+    """The reference's CPU path on the first n queries of rank 0 (n sized for about
+    args.cpu_seconds of CPU work, at most n_max)."""
     threads = host_threads()
     os.environ["TRIDENT_REF_THREADS"] = str(threads)
-    probe_n = min(cfg.B, 8)
+    probe_n = min(n_max, 8)
     dt, _, _ = cpu_reference_run(xq, c_np, cfg.nprobe, cfg.K, xs, perm, off, probe_n, threads)
     per_q = dt / probe_n
-    n = int(max(16, min(cfg.B, args.cpu_seconds / max(per_q, 1e-6))))
+    n = int(max(min(16, n_max), min(n_max, args.cpu_seconds / max(per_q, 1e-6))))
     dt, _, _ = cpu_reference_run(xq, c_np, cfg.nprobe, cfg.K, xs, perm, off, n, threads)
     return {"value": n / dt, "unit": UNIT, "cores": threads, "kind": "reference",
-            "sample": f"first {n} of the {cfg.B} queries (one call: float64 probe selection + "
+            "sample": f"first {n} of rank 0's {xq.shape[0]} queries (one call: float64 probe selection + "
                       f"omp_cpu_ivfflat_f32 with {threads} threads), {dt:.2f}s"}
 
 
-def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks):
-    """Algorithmic bytes of the main scan launch (pass 1) under each query's final K-th distance,
-    divided by its measured duration. bytes = B*D_pad*4 (rotated queries) + per distinct probed list
-    (4 B per row id + 3*D_pad*4 B of vmin/delta/eps) + per row 32 B x the largest number of 32-dim
-    blocks any query must scan + D*4 B per distinct surviving row + 8 B per candidate slot written."""
+def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks, list_stride=0):
+    """Algorithmic bytes of the scan launch under each query's final K-th distance, divided by its
+    measured duration. bytes = B*D_pad*4 (rotated queries) + per distinct probed list (4 B per row id
+    + 3*D_pad*4 B of vmin/delta/eps) + per row 32 B x the largest number of 32-dim blocks any query
+    must scan + D*4 B per distinct surviving row + 8 B per candidate slot written.
+    list_stride > 1 profiles only the lists c with c % list_stride == 0 (all queries probing them)
+    and scales the per-row terms by the probed rows' total over the sampled lists' rows."""
     import numpy as np
     import torch
 
@@ -318,38 +389,63 @@ def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks):
 
     cids, _, qrot = idx.coarse(xq_dev, cfg.nprobe)
     torch.cuda.synchronize()
-    cids = cids.cpu().numpy()
-    from trident_b200 import _lib
-
-    p1 = np.ascontiguousarray(cids)
-    h = {"vec_off": idx.storage.cluster_vec_off.cpu().numpy(), "tile_off": idx.cluster_tile_off.cpu().numpy()}
+    p1 = np.ascontiguousarray(cids.cpu().numpy())
+    vec_off = idx.storage.cluster_vec_off.cpu().numpy()
+    tile_off = idx.cluster_tile_off.cpu().numpy()
+    L = np.diff(vec_off)
+    lists = np.unique(p1[p1 >= 0])
+    nb, T = idx.num_blocks, idx.tile_size
     tau = out_d[:, cfg.K - 1].astype(np.float32)
     t0 = time.perf_counter()
+    if list_stride > 1:  # compact copies of the sampled lists' codes, other lists empty
+        samp = lists[lists % list_stride == 0]
+        keep = np.zeros(idx.nlist, bool)
+        keep[samp] = True
+        p1s = np.where(keep[np.maximum(p1, 0)] & (p1 >= 0), p1, -1).astype(np.int32)
+        cnt = np.where(keep, L, 0)
+        s_off = np.zeros(idx.nlist + 1, np.int64)
+        s_off[1:] = np.cumsum(cnt)
+        tiles = np.where(keep, np.diff(tile_off), 0)
+        s_toff = np.zeros(idx.nlist + 1, np.int64)
+        s_toff[1:] = np.cumsum(tiles)
+        tile_ids = np.concatenate([np.arange(tile_off[c], tile_off[c + 1]) for c in samp]) if len(samp) else \
+            np.zeros(0, np.int64)
+        per_tile = nb * T * 32
+        codes = idx.codes.view(-1, per_tile)[torch.from_numpy(tile_ids).to(idx.codes.device)].cpu().numpy()
+        scale = float(L[lists].sum()) / max(1.0, float(L[samp].sum()))
+        prof_lists, prof_off = samp, s_off
+    else:
+        p1s, s_off, s_toff, codes, scale = p1, vec_off, tile_off, idx.codes.cpu().numpy(), 1.0
+        prof_lists, prof_off = lists, vec_off
     cand, blocks, surv, rows = O.stage_y_profile(
-        p1, h["vec_off"], h["tile_off"], idx.tile_size, idx.codes.cpu().numpy(), idx.vmin_pad.cpu().numpy(),
-        idx.delta_pad.cpu().numpy(), idx.eps_pad.cpu().numpy(), qrot.cpu().numpy(), tau, want_rows=True)
+        p1s, s_off, s_toff, T, codes.reshape(-1), idx.vmin_pad.cpu().numpy(), idx.delta_pad.cpu().numpy(),
+        idx.eps_pad.cpu().numpy(), qrot.cpu().numpy(), tau, want_rows=True)
     prof_s = time.perf_counter() - t0
-    nb = idx.num_blocks
-    lists = np.unique(p1)
-    L = np.diff(h["vec_off"])
-    in_lists = np.zeros(idx.N, bool)
-    for c in lists:
-        in_lists[h["vec_off"][c]:h["vec_off"][c + 1]] = True
+    in_lists = np.zeros(int(prof_off[-1]), bool)
+    for c in prof_lists:
+        in_lists[prof_off[c]:prof_off[c + 1]] = True
     rb = rows[in_lists]
-    surv_rows = int((rb > nb).sum())
-    code_bytes = int(32 * np.minimum(rb, nb).astype(np.int64).sum())
+    surv_rows = int(round((rb > nb).sum() * scale))
+    code_bytes = int(round(32 * np.minimum(rb, nb).astype(np.int64).sum() * scale))
     bytes_alg = (cfg.B * idx.D_pad * 4 + int(L[lists].sum()) * 4 + len(lists) * 3 * idx.D_pad * 4 + code_bytes
-                 + surv_rows * idx.D * 4 + p1.size * cfg.K * 8)
+                 + surv_rows * idx.D * 4 + int((p1 >= 0).sum()) * cfg.K * 8)
+    B_here = int(xq_dev.shape[0])
+    bytes_alg += (B_here - cfg.B) * idx.D_pad * 4
     achieved = bytes_alg / (scan_ms * 1e-3) / 1e9
     peak = float(peaks.get("hbm_gbs", 6650.0))
-    return {
+    out = {
         "bound": "hbm", "kernel": "scan_kernel (Stage Y/Z over every probe)", "achieved": round(achieved, 1),
-        "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(),
+        "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(cfg.name),
         "algorithmic_bytes": int(bytes_alg), "launch_ms": round(scan_ms, 4),
         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback 6.65 TB/s",
-        "pairs": int(p1.size), "candidates": int(cand.sum()), "blocks": int(blocks.sum()),
-        "survivor_pairs": int(surv.sum()), "survivor_rows": surv_rows, "profile_s": round(prof_s, 2),
+        "pairs": int((p1 >= 0).sum()), "candidates": int(round(cand.sum() * scale)),
+        "blocks": int(round(blocks.sum() * scale)), "survivor_pairs": int(round(surv.sum() * scale)),
+        "survivor_rows": surv_rows, "profile_s": round(prof_s, 2),
     }
+    if list_stride > 1:
+        out["profile_sample"] = (f"lists c with c % {list_stride} == 0 ({len(prof_lists)} of {len(lists)} probed "
+                                 f"lists), per-row terms scaled by {scale:.3f}")
+    return out
 
 
 def pcie_accounting(idx, cfg, xq_dev, nprobe, K, mode, ub_seed, ms_per_step):
@@ -372,17 +468,19 @@ def pcie_accounting(idx, cfg, xq_dev, nprobe, K, mode, ub_seed, ms_per_step):
             "pcie_nominal_gbs": 64.0, "pcie_frac_of_nominal": round(gbs / 64.0, 4)}
 
 
-def traffic_from_profile():
-    """DRAM bytes per launch of the scan kernel from the committed ncu summary, if any."""
-    path = os.path.join(ROOT, "profiles", "scan_kernel_c2.md")
-    if not os.path.exists(path):
-        return None
-    for line in open(path):
-        if line.strip().startswith("dram_bytes_per_launch:"):
-            try:
-                return int(float(line.split(":", 1)[1].strip()))
-            except ValueError:
-                return None
+def traffic_from_profile(workload: str):
+    """DRAM bytes per scan launch at `workload` from the committed ncu summary of that workload
+    (a line `dram_bytes_per_launch[<workload>]: <bytes>`), or None when no capture of it is committed."""
+    import glob
+
+    key = f"dram_bytes_per_launch[{workload}]:"
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", "scan_kernel_*.md"))):
+        for line in open(path):
+            if line.strip().startswith(key):
+                try:
+                    return int(float(line.split(":", 1)[1].strip()))
+                except ValueError:
+                    return None
     return None
 
 
@@ -406,9 +504,12 @@ def run_ours(args, d: Dist):
     from trident_b200 import _lib
     from trident_b200.shard import ShardedSearch
 
-    cfg, xb, xq, c_np, l_np, idx = make_workload(args, d)
-    B, K, nprobe = cfg.B, cfg.K, cfg.nprobe
-    mode = args.mode if args.mode != -1 else idx.route(B, nprobe)
+    from oracle import oracle as O
+
+    cfg, xq, c_np, l_np, idx, strong = make_workload(args, d)
+    B, K, nprobe = int(xq.shape[0]), cfg.K, cfg.nprobe  # B: this rank's queries per step
+    # the scan of a step covers every rank's queries over this rank's lists
+    mode = args.mode if args.mode != -1 else idx.route(B * d.world, nprobe)
     xq_pin = torch.from_numpy(xq).pin_memory()
     xq_dev = xq_pin.to(d.dev)
     sharded = ShardedSearch(idx) if d.world > 1 else None
@@ -423,10 +524,27 @@ def run_ours(args, d: Dist):
     d_out, i_out = step(xq_dev)
     torch.cuda.synchronize()
     got_d, got_i = d_out.cpu().numpy(), i_out.cpu().numpy()
+    if d.world > 1:  # every rank's queries and results, for rank 0's roofline of its scan
+        import torch.distributed as dist
+
+        xq_all_dev = torch.empty((B * d.world, cfg.D), dtype=torch.float32, device=d.dev)
+        dist.all_gather_into_tensor(xq_all_dev, xq_dev)
+        d_all_dev = torch.empty((B * d.world, K), dtype=torch.float32, device=d.dev)
+        dist.all_gather_into_tensor(d_all_dev, d_out.contiguous())
+        d_all = d_all_dev.cpu().numpy()
+    else:
+        xq_all_dev, d_all = xq_dev, got_d
     xs = perm = off = None
     check = None
+    n_cpu = 0 if args.no_cpu_baseline else min(B, CPU_SAMPLE_CAP.get(cfg.name.split("_")[0], B))
     if d.rank == 0:
-        xs, perm, off = host_storage(xb, l_np, cfg.nlist)
+        # host rows of every list that the checked queries and the CPU-baseline sample probe
+        t0 = time.perf_counter()
+        n_need = min(B, max(args.check, n_cpu))
+        cids_need, _ = O.probe_select_f64(xq[:n_need], c_np, nprobe)
+        xs, perm, off = host_storage(cfg, l_np, np.unique(cids_need[cids_need >= 0]), d.dev)
+        log(f"[rank 0] host rows of the {n_need} sample queries' lists: {xs.shape[0]} rows in "
+            f"{time.perf_counter() - t0:.1f}s")
         check = check_against_oracle(cfg, xq, c_np, xs, perm, off, got_d, got_i, args.check)
         log(f"[rank 0] oracle check: {check}")
         if not (check["ids_identical"] and check["distances_bit_identical"]):
@@ -521,21 +639,27 @@ def run_ours(args, d: Dist):
         ms_per_step = total_ms / args.steps
         scan_ms = phase_tot.get("scan", 0.0) / args.steps
         roof = None
-        if not args.no_roofline and d.world == 1 and mode == 2:
-            roof = roofline(idx, cfg, xq_dev, got_d, scan_ms, peaks)
+        if not args.no_roofline and mode == 2:
+            # rank 0's scan covers every rank's queries over rank 0's lists
+            stride = 64 if cfg.nlist > 8192 else 1
+            roof = roofline(idx, cfg, xq_all_dev, d_all, scan_ms, peaks, list_stride=stride)
+            if d.world > 1:
+                roof["scope"] = f"rank 0's scan: all {B * d.world} queries over rank 0's lists"
         cpu = None
-        if not args.no_cpu_baseline and d.world == 1:
-            cpu = cpu_baseline(args, cfg, xq, c_np, xs, perm, off)
+        if n_cpu:
+            cpu = cpu_baseline(args, cfg, xq, c_np, xs, perm, off, n_cpu)
         ooc = None
         if args.ooc and d.world == 1:
             ooc = pcie_accounting(idx, cfg, xq_dev, nprobe, K, mode, args.ub_seed, ms_per_step)
         result = {
             "metric": METRIC, "value": round(B * d.world / (ms_per_step * 1e-3), 1), "unit": UNIT,
             "n_gpus": d.world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded GIST1M-shaped decay-spectrum rows, generated on the GPU)",
+            "higher_is_better": True, "scaling": "strong" if strong else "weak", "vs_baseline": None,
+            "dtype": "f32",
+            "data": data_desc(cfg),
             "config": {
-                "workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} nprobe={nprobe} K={K} B={B} per GPU",
+                "workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} nprobe={nprobe} K={K} " +
+                            (f"B={B * d.world} in total" if strong else f"B={B} per GPU"),
                 "global_batch": B * d.world,
                 "mode": {2: "cascade", 10: "cm_fp32"}[mode] + (" (router)" if args.mode == -1 else ""),
                 "ub_seed": args.ub_seed, "tile_size": idx.tile_size,
@@ -570,15 +694,22 @@ def run_reference(args, d: Dist):
         ref_cpu.load()
     except Exception as e:
         return {"impl": "reference", "unavailable": f"reference CPU module not built: {e}"}
-    cfg, xb, xq, c_np, l_np, idx = make_workload(args, d)
-    xs, perm, off = host_storage(xb, l_np, cfg.nlist)
-    del idx, xb
+    import numpy as np
+
+    from oracle import oracle as O
+
+    cfg = workload_config(args)
+    xb, xq, lids, c_np, l_np, _, _, strong = make_clustering(args, d, cfg)
+    del xb, lids
     torch.cuda.empty_cache()
+    n_max = min(xq.shape[0], CPU_SAMPLE_CAP.get(cfg.name.split("_")[0], xq.shape[0]))
+    cids_need, _ = O.probe_select_f64(xq[:n_max], c_np, cfg.nprobe)
+    xs, perm, off = host_storage(cfg, l_np, np.unique(cids_need[cids_need >= 0]), d.dev)
     threads = host_threads()
     os.environ["TRIDENT_REF_THREADS"] = str(threads)
-    dt, _, _ = cpu_reference_run(xq, c_np, cfg.nprobe, cfg.K, xs, perm, off, min(cfg.B, 8), threads)
+    dt, _, _ = cpu_reference_run(xq, c_np, cfg.nprobe, cfg.K, xs, perm, off, min(n_max, 8), threads)
     budget_s = 150.0 / max(args.steps + args.warmup, 1)
-    n = int(max(8, min(cfg.B, budget_s / max(dt / min(cfg.B, 8), 1e-6))))
+    n = int(max(min(8, n_max), min(n_max, budget_s / max(dt / min(n_max, 8), 1e-6))))
     for _ in range(args.warmup):
         cpu_reference_run(xq, c_np, cfg.nprobe, cfg.K, xs, perm, off, n, threads)
     times = []
@@ -590,9 +721,11 @@ def run_reference(args, d: Dist):
     return {
         "metric": METRIC, "value": round(qps, 2), "unit": UNIT, "n_gpus": getattr(d, "launched", d.world), "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(tot / args.steps * 1e3, 2), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32", "data": data_desc(cfg),
+        "impl": "reference",
         "config": {"workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} nprobe={cfg.nprobe} "
-                               f"K={cfg.K} B={cfg.B} per GPU", "global_batch": cfg.B * getattr(d, "launched", d.world),
+                               f"K={cfg.K} " + (f"B={cfg.B} in total" if strong else f"B={cfg.B} per GPU"),
+                   "global_batch": cfg.B if strong else cfg.B * getattr(d, "launched", d.world),
                    "host": "rank 0's host cores only: the reference's CPU path does not use the GPUs",
                    "sample_queries_per_step": n},
         "cpu_baseline": {"value": round(qps, 2), "unit": UNIT, "cores": threads, "kind": "reference",

@@ -6,8 +6,9 @@ distributions: NumPy PCG64 on the host (tests, fixtures, CPU-sized cases) and to
 CUDA device (benchmark-sized cases). They draw different numbers; the stored arrays, not the
 generator, are the ground truth every check uses.
 
-Seeds: base rows 0, queries 1, k-means 2, PCA sample 3; mixture centres 100 (shared by base rows and
-queries, so both come from the same distribution).
+Seeds: base rows 0, queries 1, k-means 2, PCA sample 3; mixture centres 100. The centres are always
+drawn by NumPy (PCG64, seed 100), whichever generator draws the rows, so base rows generated on the
+GPU and queries generated on the host come from the same mixture.
 """
 from dataclasses import dataclass, field
 from typing import Optional, Tuple
@@ -102,25 +103,42 @@ def generate_np(cfg: Config, n: int, seed: int, chunk: int = 65_536) -> np.ndarr
 # torch generator (CUDA device)
 # ----------------------------------------------------------------------------------------------
 def _torch_centres(cfg: Config, device):
+    """The mixture centres of the NumPy generator (PCG64, seed SEED_CENTRES), moved to `device`: rows
+    drawn on the GPU and queries drawn on the host must come from the same mixture."""
     import torch
 
-    g = torch.Generator(device=device)
-    g.manual_seed(SEED_CENTRES)
-    if cfg.kind == "int_mixture":
-        return torch.rand((cfg.n_comp, cfg.D), generator=g, device=device, dtype=torch.float64) * 255.0
-    if cfg.kind == "norm_mixture":
-        return torch.randn((cfg.n_comp, cfg.D), generator=g, device=device, dtype=torch.float64)
-    return None
+    if cfg.kind not in ("int_mixture", "norm_mixture"):
+        return None
+    return torch.from_numpy(_np_centres(cfg)).to(device)
 
 
-def generate_torch(cfg: Config, n: int, seed: int, device="cuda", chunk: int = 1 << 20, out=None):
+TORCH_CHUNK = 1 << 20  # rows per generator call; regeneration must use the same chunking
+
+
+def iter_torch_chunks(cfg: Config, n: int, seed: int, device="cuda", chunk: int = TORCH_CHUNK):
+    """Yields (start, end, rows [end - start, D] float32 on `device`) for rows [0, n) of cfg's
+    distribution, in order. The draws depend only on (cfg, seed, chunk), so a second pass yields the
+    same rows: a process can regenerate the rows it needs instead of keeping them."""
+    for s, e, x in _torch_rows(cfg, n, seed, device, chunk):
+        yield s, e, x
+
+
+def generate_torch(cfg: Config, n: int, seed: int, device="cuda", chunk: int = TORCH_CHUNK, out=None):
     """n rows of cfg's distribution as a float32 tensor [n, D] on `device` (or written into `out`)."""
+    import torch
+
+    if out is None:
+        out = torch.empty((n, cfg.D), dtype=torch.float32, device=device)
+    for s, e, x in _torch_rows(cfg, n, seed, device, chunk):
+        out[s:e].copy_(x)
+    return out
+
+
+def _torch_rows(cfg: Config, n: int, seed: int, device, chunk: int):
     import torch
 
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    if out is None:
-        out = torch.empty((n, cfg.D), dtype=torch.float32, device=device)
     centres = _torch_centres(cfg, device)
     scale = (torch.arange(cfg.D, device=device, dtype=torch.float64) + 1.0) ** (-cfg.alpha)
     for s in range(0, n, chunk):
@@ -139,8 +157,7 @@ def generate_torch(cfg: Config, n: int, seed: int, device="cuda", chunk: int = 1
             x = x / torch.linalg.norm(x, dim=1, keepdim=True)
         else:
             raise ValueError(cfg.kind)
-        out[s:e].copy_(x.to(torch.float32))
-    return out
+        yield s, e, x.to(torch.float32)
 
 
 def make_dataset(cfg: Config, device=None) -> Tuple[object, object]:
