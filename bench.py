@@ -680,6 +680,7 @@ def run_ours(args, d: Dist):
             "roofline": roof, "cpu_baseline": cpu,
             **({"ooc": ooc} if ooc is not None else {}),
         }
+    d.barrier()  # rank 0's post-timing checks end before any rank leaves the process group
     return result
 
 

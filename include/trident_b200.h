@@ -209,6 +209,18 @@ int trident_search_noalloc(const trident_index* idx, const float* xq, int32_t B,
  * header's macro). */
 size_t trident_noalloc_workspace_bytes(void);
 
+/* Index build: the nearest centroid of each row, out[i] = argmin_c (cnorm[c] - 2 x_i.c) (ties to the
+ * smaller c), on the tensor cores (TF32 products, the TMA-fed GEMM of the coarse stage with an argmin
+ * epilogue). Replaces the reference's faiss assignment (benchmarks/phase4a_suite.py:389-421, the
+ * k-means training and list assignment of load_or_train_clustering). The list assignment is an input
+ * of the index; searches are exact for whatever assignment they are given, so TF32 rounding near a
+ * tie only moves a row between two equally near lists.
+ *   x [n, D] and centroids [nlist, D] float32 row-major on the device, 16-byte aligned, D % 4 == 0;
+ *   cnorm [nlist] = ||c||^2; out [n] int32; dev_status: one device int32 that receives
+ *   TRIDENT_STATUS_MMA_TIMEOUT (or-ed in) if a bounded wait gave up (out is then incomplete). */
+int trident_assign(const float* x, int64_t n, int32_t D, const float* centroids, const float* cnorm, int32_t nlist,
+                   int32_t* out, int32_t* dev_status, void* stream);
+
 /* Per-query side information of trident_search_prep: [B, TRIDENT_QINFO_LEN] float32 (||q||,
  * the bound's query slack sigma, ||q - mu||, padding). */
 #define TRIDENT_QINFO_LEN 4

@@ -27,7 +27,7 @@ EXPORTED = (
     "trident_route", "trident_search", "trident_search_profiled", "trident_launch_count", "trident_coarse",
     "trident_merge_shards", "trident_search_noalloc", "trident_search_prep", "trident_search_seed",
     "trident_search_finish", "trident_workspace_status", "trident_set_wait_limits",
-    "trident_noalloc_workspace_bytes",
+    "trident_noalloc_workspace_bytes", "trident_assign",
 )
 QINFO_LEN = 4
 PHASES = ("coarse", "pairs", "seed", "scan", "merge")
@@ -110,10 +110,11 @@ def lib():
     L.trident_workspace_status.argtypes = [P, P, ctypes.POINTER(i32)]
     L.trident_set_wait_limits.argtypes = [i64, i64]
     L.trident_noalloc_workspace_bytes.restype = sz
+    L.trident_assign.argtypes = [P, i64, i32, P, P, i32, P, P, P]
     for name in ("trident_index_check", "trident_workspace_size", "trident_search", "trident_search_profiled",
                  "trident_coarse", "trident_merge_shards", "trident_search_noalloc", "trident_search_prep",
                  "trident_search_seed", "trident_search_finish", "trident_workspace_status",
-                 "trident_set_wait_limits"):
+                 "trident_set_wait_limits", "trident_assign"):
         getattr(L, name).restype = ctypes.c_int
     _LIB = L
     return L

@@ -50,8 +50,15 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
     if ptxas_info:
         flags.insert(0, "-Xptxas=-v")
 
+    headers = glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(CSRC, "*.h")) + \
+        glob.glob(os.path.join(INCLUDE, "*.h"))
+    newest_header = max([os.path.getmtime(h) for h in headers] + [os.path.getmtime(__file__)])
+
     def compile_one(src):
         obj = os.path.join(objdir, os.path.splitext(os.path.basename(src))[0] + ".o")
+        if not force and not ptxas_info and os.path.exists(obj) and \
+                os.path.getmtime(obj) > max(os.path.getmtime(src), newest_header):
+            return obj  # up to date
         cmd = [nvcc(), *flags, "-c", src, "-o", obj]
         if verbose:
             print(" ".join(cmd), flush=True)

@@ -29,12 +29,41 @@ def _as_tensor(x, device):
     return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(device)
 
 
+def assign_tc(x, centroids):
+    """Nearest centroid of every row on the tensor cores (trident_assign: the coarse stage's TMA-fed
+    tcgen05 GEMM with an argmin epilogue, TF32 products). x and centroids: contiguous float32 CUDA
+    tensors with D % 4 == 0. Returns int32 list ids."""
+    torch = _torch()
+    from . import _lib
+
+    n, D = (int(v) for v in x.shape)
+    cn = (centroids.double() ** 2).sum(1).float().contiguous()
+    out = torch.empty(n, dtype=torch.int32, device=x.device)
+    status = torch.zeros(1, dtype=torch.int32, device=x.device)
+    stream = torch.cuda.current_stream(x.device)
+    _lib.check(_lib.lib().trident_assign(x.data_ptr(), n, D, centroids.data_ptr(), cn.data_ptr(),
+                                         int(centroids.shape[0]), out.data_ptr(), status.data_ptr(),
+                                         stream.cuda_stream))
+    if int(status.item()) != 0:
+        raise RuntimeError(f"trident_assign: a bounded wait gave up (status {int(status.item())})")
+    return out
+
+
+def _tc_ok(x, centroids) -> bool:
+    return (x.is_cuda and x.dtype == centroids.dtype == _torch().float32 and x.is_contiguous()
+            and centroids.is_contiguous() and x.shape[1] % 4 == 0 and x.data_ptr() % 16 == 0
+            and centroids.data_ptr() % 16 == 0)
+
+
 def assign(x, centroids, chunk: int = 1 << 16, tf32: bool = False):
     """Nearest centroid (squared L2 via ||c||^2 - 2 x.c; ties to the smaller id). Returns int64 list
-    ids on x's device. With tf32 the product runs on the TF32 tensor cores: the list assignment is
-    an input of the index (the search is exact for whatever assignment it is given), so it does not
-    need float32 rounding, and large builds run several times faster."""
+    ids on x's device. With tf32 the products run on the TF32 tensor cores (trident_assign on CUDA
+    when the layout allows, else torch with TF32 matmuls): the list assignment is an input of the
+    index (the search is exact for whatever assignment it is given), so it does not need float32
+    rounding, and large builds run many times faster."""
     torch = _torch()
+    if tf32 and _tc_ok(x, centroids):
+        return assign_tc(x, centroids).long()
     cn = (centroids.double() ** 2).sum(1).float()
     out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
     ct = centroids.t().contiguous()

@@ -87,6 +87,7 @@ size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void*
     w.qinfo = (float*)take(Bs * QI_LEN * sizeof(float));
     w.coarse = (float*)take(Bs * (size_t)idx.nlist * sizeof(float));
     w.tilemin = (float*)take(Bs * (size_t)((idx.nlist + kCoarseTileN - 1) / kCoarseTileN) * sizeof(float));
+    w.gsplit = (float*)take(coarse_split_bytes(idx, (int)Bs));
     w.probe = (int32_t*)take(pairs * sizeof(int32_t));
     w.cnt = (int32_t*)take(2 * (size_t)idx.nlist * sizeof(int32_t));
     w.off = (int32_t*)take(2 * (size_t)(idx.nlist + 1) * sizeof(int32_t));
@@ -198,7 +199,7 @@ int trident_coarse(const trident_index* idx, const float* xq, int32_t B, int32_t
     cudaStream_t st = (cudaStream_t)stream;
     TB_TRY(cudaMemsetAsync(ws.ctr, 0, 16 * sizeof(int32_t), st), "memset counters");
     TB_TRY(launch_rotate(*idx, xq, B, ws.qrot, ws.qinfo, ws.tau, st), "rotate");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.tilemin, ws.ctr + kStatusWord, st), "coarse_gemm");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.tilemin, ws.gsplit, ws.ctr + kStatusWord, st), "coarse_gemm");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.tilemin, ws.qinfo, probe_cids, probe_d64,
                                (unsigned long long*)stats, ws.ctr + kStatusWord, st),
            "probe_select");
@@ -264,7 +265,7 @@ static int stage_coarse(const trident_index* idx, const float* xq, int32_t B, in
     TB_TRY(cudaStreamWaitEvent(ss->s, ss->fork, 0), "fork");
     TB_TRY(launch_rotate_f64(*idx, xq, B, ws.qrot, ss->s), "rotate");
     TB_TRY(cudaEventRecord(ss->join, ss->s), "join");
-    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.tilemin, ws.ctr + kStatusWord, st), "coarse_gemm");
+    TB_TRY(launch_coarse_gemm(*idx, xq, B, ws.coarse, ws.tilemin, ws.gsplit, ws.ctr + kStatusWord, st), "coarse_gemm");
     TB_TRY(launch_probe_select(*idx, xq, B, nprobe, ws.coarse, ws.tilemin, ws.qinfo, ws.probe, nullptr, sp, ws.ctr + kStatusWord,
                                st),
            "probe_select");
@@ -491,6 +492,21 @@ int trident_search_finish(const trident_index* idx, const float* xq, int32_t B, 
     const Marker nomark{nullptr, st};
     return stage_scan(idx, xq, B, K, nprobe, mode == TRIDENT_MODE_CASCADE, ub_seed, ws, out_d, out_i,
                       (unsigned long long*)stats, st, nomark);
+}
+
+int trident_assign(const float* x, int64_t n, int32_t D, const float* centroids, const float* cnorm, int32_t nlist,
+                   int32_t* out, int32_t* dev_status, void* stream) {
+    if (n < 0 || n >= ((int64_t)1 << 31)) return fail(TRIDENT_ERR_UNSUPPORTED, "n=%lld outside [0, 2^31)", (long long)n);
+    if (D < 4 || D > kMaxD || (D % 4) != 0) return fail(TRIDENT_ERR_UNSUPPORTED, "D=%d must be a multiple of 4 in [4, %d]", D, kMaxD);
+    if (nlist < 1) return fail(TRIDENT_ERR_INVALID, "nlist=%d", nlist);
+    if (n == 0) return TRIDENT_OK;
+    if (!x || !centroids || !cnorm || !out || !dev_status) return fail(TRIDENT_ERR_INVALID, "NULL buffer");
+    if ((((uintptr_t)x) | ((uintptr_t)centroids)) & 15) return fail(TRIDENT_ERR_INVALID, "x / centroids must be 16-byte aligned");
+    cudaError_t e = launch_assign(x, n, D, centroids, cnorm, nlist, out, dev_status, (cudaStream_t)stream);
+    if (e == cudaErrorNotSupported) return fail(TRIDENT_ERR_UNSUPPORTED, "tensor maps unavailable for this layout");
+    TB_TRY(e, "assign");
+    g_launches += 1;
+    return TRIDENT_OK;
 }
 
 int trident_merge_shards(const float* d_in, const int64_t* i_in, int32_t R, int32_t B, int32_t K, float* out_d,

@@ -339,8 +339,10 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
     }
     const bool cached = nlist <= kSelSmemKeys;
     for (int d = tid; d < D; d += blockDim.x) qv[d] = xq[(int64_t)j * D + d];
-    if (cached)
+    if (cached) {
+#pragma unroll 8
         for (int c = tid; c < nlist; c += blockDim.x) skeys[c] = float_key(__ldg(row + c));
+    }
     __syncthreads();
 
     // 1) t >= the nprobe-th smallest approximate value (equal to it except on the tile-minimum path)
@@ -426,9 +428,7 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
     // the chunked pass below takes them in batches instead.
     if (tid == 0) s_n = 0;
     __syncthreads();
-    for (int c0 = warp * 32; c0 < nlist; c0 += kSelThreads) {  // warp-uniform trip count
-        const int c = c0 + lane;
-        const bool mem = (c < nlist) && ((cached ? key_float(skeys[c]) : __ldg(row + c)) <= thr);
+    auto offer = [&](bool mem, int c) {  // warp-aggregated append of the members among 32 lanes
         const unsigned m = __ballot_sync(TB_FULL, mem);
         if (m) {
             const int leader = __ffs(m) - 1;
@@ -436,6 +436,34 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
             if (lane == leader) pos = atomicAdd(&s_n, __popc(m));
             pos = __shfl_sync(TB_FULL, pos, leader) + __popc(m & ((1u << lane) - 1u));
             if (mem && pos < kSelCap) scid[pos] = c;
+        }
+    };
+    if (!cached && (nlist & 3) == 0 && ((uintptr_t)row & 15) == 0) {
+        // the row from global memory: 16-byte loads, four in flight per lane (512 lists per warp step)
+        constexpr int kU = 4;
+        const float4* row4 = reinterpret_cast<const float4*>(row);
+        const int n4 = nlist >> 2;
+        for (int b4 = warp * 32 * kU; b4 < n4; b4 += kSelThreads * kU) {  // warp-uniform trip count
+            float4 v[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int i4 = b4 + u * 32 + lane;
+                v[u] = i4 < n4 ? __ldg(row4 + i4) : make_float4(kInf, kInf, kInf, kInf);
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const int c = 4 * (b4 + u * 32 + lane);
+                const bool in = c < nlist;  // (nlist % 4 == 0: the whole float4 is in range or none)
+                offer(in && v[u].x <= thr, c);
+                offer(in && v[u].y <= thr, c + 1);
+                offer(in && v[u].z <= thr, c + 2);
+                offer(in && v[u].w <= thr, c + 3);
+            }
+        }
+    } else {
+        for (int c0 = warp * 32; c0 < nlist; c0 += kSelThreads) {  // warp-uniform trip count
+            const int c = c0 + lane;
+            offer((c < nlist) && ((cached ? key_float(skeys[c]) : __ldg(row + c)) <= thr), c);
         }
     }
     __syncthreads();

@@ -25,6 +25,7 @@ struct Workspace {
     float* qinfo;       // [B, QI_LEN]
     float* coarse;      // [B, nlist] approximate ||c||^2 - 2 q.c
     float* tilemin;     // [B, ceil(nlist / kCoarseTileN)] minimum of each row over each GEMM tile
+    float* gsplit;      // coarse_split_bytes(idx, B): TF32 hi/lo splits of queries and centroids
     int32_t* probe;     // [B, nprobe]
     int32_t* cnt;       // [2, nlist]
     int32_t* off;       // [2, nlist + 1]
@@ -56,11 +57,17 @@ cudaError_t launch_query_norms(const trident_index& idx, const float* xq, int B,
 cudaError_t launch_rotate_f64(const trident_index& idx, const float* xq, int B, float* qrot, cudaStream_t st);
 cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
                           uint32_t* tau, cudaStream_t st);
-// tcgen05 3xTF32 GEMM (tb_coarse_mma.cu); sets *err = TRIDENT_STATUS_MMA_TIMEOUT if a bounded wait
-// gave up.
-// tilemin (optional, [B, ceil(nlist / kCoarseTileN)]) receives each row's minimum over each tile.
+// Persistent TMA-fed tcgen05 GEMM (tb_gemm.cu), 3xTF32; sets *err |= TRIDENT_STATUS_MMA_TIMEOUT if a
+// bounded wait gave up. tilemin (optional, [B, ceil(nlist / kCoarseTileN)]) receives each row's
+// minimum over each tile; splits is scratch of coarse_split_bytes(idx, B) bytes for the operands'
+// TF32 hi/lo splits.
+size_t coarse_split_bytes(const trident_index& idx, int B);
 cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, float* tilemin,
-                               int32_t* err, cudaStream_t st);
+                               float* splits, int32_t* err, cudaStream_t st);
+// The same GEMM with an argmin epilogue (1xTF32): out[i] = argmin_c (cnorm[c] - 2 x_i.c), ties to the
+// smaller c. Needs D % 4 == 0 and 16-byte aligned x and cent.
+cudaError_t launch_assign(const float* x, int64_t n, int D, const float* cent, const float* cnorm, int nlist,
+                          int32_t* out, int32_t* err, cudaStream_t st);
 // Exact probe lists. A nonzero *err (the GEMM gave up) marks every probe list -1 (and probe_d64 NaN)
 // and is copied into each query's qinfo[QI_PAD], which travels with the query to other GPUs.
 // tilemin (optional) lets selection above 8192 lists bound the nprobe-th value without re-reading
