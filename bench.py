@@ -61,6 +61,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-roofline", action="store_true")
     p.add_argument("--n", type=int, default=0, help="override N (rows) for quick runs")
+    p.add_argument("--sweep", action="store_true",
+                   help="c3: time both modes and the router over B x nprobe x K, oracle-checking every cell")
     a = p.parse_args()
     if a.ub_seed < 0:  # out of core, seed from SQ8 upper bounds: the seed then reads no FP32 row
         a.ub_seed = 1 if a.ooc else 0
@@ -194,7 +196,9 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------------------------
 STRONG = ("c4", "c5")  # configs whose query count is the job's total (split across ranks)
-CPU_SAMPLE_CAP = {"c4": 1000, "c5": 100}  # CPU-baseline query prefix
+# CPU-baseline query prefix for the 10^4-query configs: the sample's probes decide how many rows must
+# be copied to host memory (100 queries at C4 probe about 32% of the lists, 16 GB of rows)
+CPU_SAMPLE_CAP = {"c4": 100, "c5": 100}
 
 
 def workload_config(args):
@@ -684,6 +688,84 @@ def run_ours(args, d: Dist):
     return result
 
 
+def run_sweep(args, d: Dist):
+    """The config's sweep (c3: B in {1, 100, 10^4}, nprobe in {32, 128}, K in {1, 10, 50, 100}) on one
+    GPU: per cell, the median step time of the cascade, the CM-FP32 scan and the router's choice
+    (CUDA events, L2 flushed between steps), an oracle check of up to 16 queries, and for the
+    cascade at B <= 100 the HBM roofline fraction of its scan phase."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+
+    cfg, xq, c_np, l_np, idx, _ = make_workload(args, d)
+    ex = cfg.extra or {}
+    Bs, nps, Ks = ex.get("B", (cfg.B,)), ex.get("nprobe", (cfg.nprobe,)), ex.get("K", (cfg.K,))
+    xq_dev = torch.from_numpy(xq).to(d.dev)
+    n_chk = 16
+    cids_need, _ = O.probe_select_f64(xq[:n_chk], c_np, max(nps))
+    xs, perm, off = host_storage(cfg, l_np, np.unique(cids_need), d.dev)
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=d.dev)
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) if os.path.exists(
+        os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+
+    def timed(q, nprobe, K, mode, iters=10):
+        for _ in range(3):
+            idx.search(q, nprobe, mode=mode, k=K)
+        ms, phases = [], {}
+        for i in range(iters):
+            flush.fill_(i & 0xFF)
+            ph = {}
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            idx.search(q, nprobe, mode=mode, k=K, phase_ms=ph)
+            b.record()
+            b.synchronize()
+            ms.append(a.elapsed_time(b))
+            for k, v in ph.items():
+                phases[k] = phases.get(k, 0.0) + v / iters
+        return statistics.median(ms), phases
+
+    cells = []
+    for B in Bs:
+        q = xq_dev[:B].contiguous()
+        for nprobe in nps:
+            for K in Ks:
+                row = {"B": B, "nprobe": nprobe, "K": K}
+                for mode, name in ((2, "cascade"), (10, "cm_fp32")):
+                    ms, ph = timed(q, nprobe, K, mode)
+                    row[f"qps_{name}"] = round(B / (ms * 1e-3), 1)
+                    row[f"ms_{name}"] = round(ms, 4)
+                    if mode == 2:
+                        scan_ms = ph.get("scan", 0.0)
+                    dd, ii, _ = idx.search(q, nprobe, mode=mode, k=K)
+                    torch.cuda.synchronize()
+                    m = min(B, n_chk)
+                    od, oi, _ = O.exact_search(xq[:m], c_np, nprobe, off, xs.numpy(), perm, K)
+                    row[f"check_{name}"] = bool(np.array_equal(ii[:m].cpu().numpy(), oi) and
+                                                np.array_equal(dd[:m].cpu().numpy().view(np.uint32), od.view(np.uint32)))
+                    if mode == 2 and B <= 100:
+                        r = roofline(idx, ds_cfg_with(cfg, B=B, nprobe=nprobe, K=K), q, dd.cpu().numpy(), scan_ms, peaks)
+                        row["cascade_scan_roofline_frac"] = r["frac"]
+                        row["cascade_scan_alg_bytes"] = r["algorithmic_bytes"]
+                        row["cascade_scan_ms"] = round(scan_ms, 4)
+                routed = idx.route(B, nprobe)
+                row["router"] = {2: "cascade", 10: "cm_fp32"}[routed]
+                row["router_picked_faster"] = bool((routed == 2) == (row["ms_cascade"] <= row["ms_cm_fp32"]))
+                cells.append(row)
+                log(f"[sweep] {row}")
+    ok = all(c["check_cascade"] and c["check_cm_fp32"] for c in cells)
+    return {"metric": METRIC, "unit": UNIT, "n_gpus": 1, "sweep_of": cfg.name, "data": data_desc(cfg),
+            "config": {"workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist}"},
+            "all_cells_match_oracle": ok, "cells": cells}
+
+
+def ds_cfg_with(cfg, **kw):
+    from trident_b200 import datasets as ds
+
+    return ds.Config(**{**cfg.__dict__, **kw})
+
+
 def run_reference(args, d: Dist):
     if d.rank != 0:
         return None
@@ -746,7 +828,12 @@ def main():
         d.world = 1
     d.init()
     try:
-        res = run_reference(args, d) if args.impl == "reference" else run_ours(args, d)
+        if args.impl == "reference":
+            res = run_reference(args, d)
+        elif args.sweep:
+            res = run_sweep(args, d)
+        else:
+            res = run_ours(args, d)
     finally:
         if args.impl != "reference":
             d.close()

@@ -110,8 +110,16 @@ int trident_workspace_size(const trident_index* idx, int32_t B, int32_t K, int32
  * thresholds from max(p_init, min(8, nprobe / 8)) nearest lists of each query. */
 int32_t trident_p_init(int32_t mode, int32_t B, int32_t K, int32_t nprobe);
 
+/* Router thresholds. The reference calibrated W0 = 9e8 on an A100 (phase4a_suite.py:1013-1035,
+ * data/phase6/auto_v2.csv). The same rule on a B200 (python -m trident_b200.calibrate: the smallest W
+ * at which the cascade is at least as fast as the CM-FP32 scan, over B = 1..1024 on the c1-c3
+ * stand-ins) finds the cascade faster at every batch size measured, down to W = 8e5 (c1, B = 1). */
+#define TRIDENT_ROUTE_W0_A100 9.0e8
+#define TRIDENT_ROUTE_W0_B200 8.0e5
+
 /* The cost router (phase4a_suite.py:1013-1035, 1079): returns TRIDENT_MODE_CM_FP32 when
- * W = B * nprobe * (N / nlist) * D < w0, else TRIDENT_MODE_CASCADE. w0 <= 0 selects 9.0e8. */
+ * W = B * nprobe * (N / nlist) * D < w0, else TRIDENT_MODE_CASCADE. w0 <= 0 selects
+ * TRIDENT_ROUTE_W0_B200. */
 int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, double w0);
 
 /* The whole query path, replacing launch_trident_v4_search (:1172-1604). The cascade runs as

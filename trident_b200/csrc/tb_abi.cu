@@ -160,7 +160,7 @@ int32_t trident_p_init(int32_t mode, int32_t B, int32_t K, int32_t nprobe) {
 
 int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, double w0) {
     if (!idx || idx->nlist < 1) return TRIDENT_MODE_CASCADE;
-    if (!(w0 > 0.0)) w0 = 9.0e8;
+    if (!(w0 > 0.0)) w0 = TRIDENT_ROUTE_W0_B200;
     const double W = (double)B * (double)nprobe * ((double)idx->N / (double)idx->nlist) * (double)idx->D;
     return W < w0 ? TRIDENT_MODE_CM_FP32 : TRIDENT_MODE_CASCADE;
 }

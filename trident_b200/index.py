@@ -289,7 +289,10 @@ class TridentV4Index:
                                                        ctypes.byref(st)))
         return int(st.value)
 
-    def route(self, B: int, nprobe: int, w0: float = 9.0e8) -> int:
+    def route(self, B: int, nprobe: int, w0: float = 0.0) -> int:
+        """The cost router: 10 (CM-FP32) if W = B * nprobe * (N / nlist) * D < w0 else 2 (cascade).
+        w0 <= 0 uses the library's B200 calibration (TRIDENT_ROUTE_W0_B200); the reference's A100
+        value was 9e8."""
         return int(_lib.lib().trident_route(self.desc(), int(B), int(nprobe), float(w0)))
 
     def search(self, xq_gpu, nprobe: int, mode: int = 2, use_l1: int = 0, rerank_m: int = 0, tile_override: int = 0,
