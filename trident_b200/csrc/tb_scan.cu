@@ -160,16 +160,29 @@ __device__ __forceinline__ float bound_block_g(const uint4 w0, const uint4 w1, c
 }
 
 constexpr float kU32 = 5.9604644775390625e-08f;  // 2^-24
-constexpr int kSCS = 196;  // floats per query of scaled block-0/1 intervals: 16 groups x 12, +4 (banks)
+constexpr int kSQS = 68;   // floats per query of scaled block-0/1 bases: 64, +4 (an odd count of 16-byte words)
+constexpr int kSIS = 128;  // floats per item of scaled block-0/1 intervals: delta' [64], then eps' [64]
 constexpr int kWB = 64;    // per-warp block-1 batch capacity
 constexpr int kWQ = 64;    // per-warp deep-queue capacity (<= 31 waiting + 32 new entries)
 
-// One 4-dim group of the scaled bound: two packed FFMA2 for u' = c * delta' + base', four
+// One 4-dim group of the scaled bound of block 1: two packed FFMA2 for u' = c * delta' + base', four
 // saturating |u'| - eps', two packed FFMA2 into the running pair of partial sums.
 __device__ __forceinline__ float2 scaled_group(const float2 c01, const float2 c23, const float4 dd, const float4 bb,
                                                const float4 ee, float2 acc) {
     const float2 u01 = __ffma2_rn(c01, make_float2(dd.x, dd.y), make_float2(bb.x, bb.y));
     const float2 u23 = __ffma2_rn(c23, make_float2(dd.z, dd.w), make_float2(bb.z, bb.w));
+    const float l0 = __saturatef(fabsf(u01.x) - ee.x), l1 = __saturatef(fabsf(u01.y) - ee.y);
+    const float l2 = __saturatef(fabsf(u23.x) - ee.z), l3 = __saturatef(fabsf(u23.y) - ee.w);
+    acc = __ffma2_rn(make_float2(l0, l1), make_float2(l0, l1), acc);
+    return __ffma2_rn(make_float2(l2, l3), make_float2(l2, l3), acc);
+}
+
+// One 4-dim group of the scaled bound of block 0, whose row terms x'' = c * delta' are formed once per
+// row and reused for every query: two packed FADD2 for u' = x'' + base', four saturating |u'| - eps',
+// two packed FFMA2 into the running pair of partial sums.
+__device__ __forceinline__ float2 scaled_group0(const float4 xd, const float4 bb, const float4 ee, float2 acc) {
+    const float2 u01 = __fadd2_rn(make_float2(xd.x, xd.y), make_float2(bb.x, bb.y));
+    const float2 u23 = __fadd2_rn(make_float2(xd.z, xd.w), make_float2(bb.z, bb.w));
     const float l0 = __saturatef(fabsf(u01.x) - ee.x), l1 = __saturatef(fabsf(u01.y) - ee.y);
     const float l2 = __saturatef(fabsf(u23.x) - ee.z), l3 = __saturatef(fabsf(u23.y) - ee.w);
     acc = __ffma2_rn(make_float2(l0, l1), make_float2(l0, l1), acc);
@@ -212,8 +225,9 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
     int32_t* s_topi = reinterpret_cast<int32_t*>(s_topd + G * KM);
     uint32_t* s_sv = reinterpret_cast<uint32_t*>(s_topi + G * KM);  // [QCAP] survivors (j, r)
     float* s_sd = reinterpret_cast<float*>(s_sv + QCAP);            // [QCAP] their exact distances
-    float* s_sc = s_sd + QCAP;                                          // [G][kSCS] scaled intervals (LB)
-    float* s_wba = s_sc + (LB ? G * kSCS : 0);                          // [NW][kWB] block-1 batch bounds
+    float* s_si = s_sd + QCAP;                                          // [kSIS] scaled delta', eps' (LB)
+    float* s_sq = s_si + (LB ? kSIS : 0);                               // [G][kSQS] scaled bases (LB)
+    float* s_wba = s_sq + (LB ? G * kSQS : 0);                          // [NW][kWB] block-1 batch bounds
     float* s_wqa = s_wba + (LB ? NW * kWB : 0);                         // [NW][kWQ] deep-queue bounds
     uint32_t* s_wqe = reinterpret_cast<uint32_t*>(s_wqa + (LB ? NW * kWQ : 0));  // [NW][kWQ] deep (j, r)
     uint8_t* s_wbl = reinterpret_cast<uint8_t*>(s_wqe + (LB ? NW * kWQ : 0));    // [NW][kWB] batch lanes
@@ -470,43 +484,53 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
             }
         }
 
-        // ---- per-query scaled intervals for blocks 0 and 1. With s_j = 1/sqrt(prune threshold),
-        // l'_d = sat(|fma(c, delta_d s_j, base_jd s_j)| - eps'_jd) <= s_j l_d (eps' adds the float32
-        // roundings of the scaled terms), and clamping at 1 only lowers the bound; the scaled
-        // threshold stays <= 1 as tau tightens. Two dims go through one packed FFMA2.
+        // ---- scaled intervals for blocks 0 and 1, one scale for every query of the item:
+        // s = 1/sqrt(the item's largest finite prune threshold), so each query's scaled threshold
+        // ts_j s^2 stays <= 1. Then l'_d = sat(|c delta_d s + base_jd s| - eps'_d) <= s l_d, where eps'_d
+        // adds the float32 roundings of the scaled terms for the largest |base_jd| of the item's
+        // queries, and clamping at 1 only lowers the bound (a clamped dim already exceeds every
+        // query's scaled threshold). delta' and eps' are the same for every query, so block 0 reads
+        // only the query's bases (base' = base s) per query.
         if (LB) {
-            const int nsc = min(nb, 2) * 8;  // 4-dim groups staged
+            const int ndim = min(nb, 2) * 32;
+            float tmax = 0.0f;
+            bool any = false;
+            for (int j = 0; j < n; ++j) {
+                const float t = s_ts[j];
+                if (t < kInf) {
+                    tmax = fmaxf(tmax, t);
+                    any = true;
+                }
+            }
+            const float sc = any ? 1.0f / sqrtf(fmaxf(tmax, 1e-30f)) : 1.0f;
             if (tid < n) {
                 const float ts = s_ts[tid];
-                const float sc = (ts < kInf) ? 1.0f / sqrtf(fmaxf(ts, 1e-30f)) : 1.0f;
                 s_scale[tid] = sc;
                 s_s2inv[tid] = (ts < kInf) ? 1.0f / (sc * sc) * (1.0f - 4.0f * kU32) : 1.0f;
                 s_tsp[tid] = (ts < kInf) ? ts * sc * sc * (1.0f + 64.0f * kU32) : kInf;
             }
+            if (tid < 64) s_si[64 + tid] = 0.0f;  // the largest |base_jd| per dim, as float bits
             __syncthreads();
-            // one 4-dim group per task; base = vmin - q~ with the same float32 subtraction as the staged copies
+            // base' = (vmin - q~_j) s with the same float32 subtraction as the staged copies
+            const int ng = ndim / 4;
 #pragma unroll 2
-            for (int i = tid; i < n * nsc; i += T) {
-                const int j = i / nsc, g = i - j * nsc;
-                const float sc = s_scale[j];
-                const int sd = (g >> 3) * kBS + 4 * (g & 7);
+            for (int i = tid; i < n * ng; i += T) {
+                const int j = i / ng, g = i - j * ng;
                 const float4 v4 = __ldg(reinterpret_cast<const float4*>(vm_c) + g);
                 const float4 q4 = __ldg(reinterpret_cast<const float4*>(a.qrot + (int64_t)s_qid[j] * D_pad) + g);
-                const float4 d4 = *reinterpret_cast<const float4*>(s_dl + sd);
-                const float4 e4 = *reinterpret_cast<const float4*>(s_ep + sd);
                 const float b[4] = {v4.x - q4.x, v4.y - q4.y, v4.z - q4.z, v4.w - q4.w};
-                const float dl[4] = {d4.x, d4.y, d4.z, d4.w}, ep[4] = {e4.x, e4.y, e4.z, e4.w};
-                float o[12];
+                reinterpret_cast<float4*>(s_sq + j * kSQS)[g] = make_float4(b[0] * sc, b[1] * sc, b[2] * sc, b[3] * sc);
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    o[k] = dl[k] * sc;
-                    o[4 + k] = b[k] * sc;
-                    o[8 + k] = (ep[k] * sc + 2.0001f * kU32 * sc * (255.0f * dl[k] + fabsf(b[k]))) * (1.0f + 3.0f * kU32);
-                }
-                float4* P = reinterpret_cast<float4*>(s_sc + j * kSCS + g * 12);
-                P[0] = make_float4(o[0], o[1], o[2], o[3]);
-                P[1] = make_float4(o[4], o[5], o[6], o[7]);
-                P[2] = make_float4(o[8], o[9], o[10], o[11]);
+                for (int k = 0; k < 4; ++k) atomicMax(reinterpret_cast<int*>(s_si + 64 + 4 * g + k), __float_as_int(fabsf(b[k])));
+            }
+            __syncthreads();
+            // delta' = delta s; eps' covers the roundings of delta', base', c delta' and u' (3u |term| each)
+            if (tid < ndim) {
+                const int sd = (tid >> 5) * kBS + (tid & 31);
+                const float dl = s_dl[sd], ep = s_ep[sd];
+                const float bm = s_si[64 + tid];
+                s_si[tid] = dl * sc;
+                s_si[64 + tid] = (ep * sc + 3.0001f * kU32 * sc * (255.0f * dl + bm)) * (1.0f + 3.0f * kU32);
             }
             __syncthreads();
         }
@@ -689,13 +713,14 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                     w[2] = __shfl_sync(TB_FULL, p0.z, r); w[3] = __shfl_sync(TB_FULL, p0.w, r);
                     w[4] = __shfl_sync(TB_FULL, p1.x, r); w[5] = __shfl_sync(TB_FULL, p1.y, r);
                     w[6] = __shfl_sync(TB_FULL, p1.z, r); w[7] = __shfl_sync(TB_FULL, p1.w, r);
-                    const float4* P = reinterpret_cast<const float4*>(s_sc + jj * kSCS) + 24;
+                    const float4* D1 = reinterpret_cast<const float4*>(s_si + 32);       // delta' of block 1
+                    const float4* E1 = reinterpret_cast<const float4*>(s_si + 64 + 32);  // eps' of block 1
+                    const float4* B1 = reinterpret_cast<const float4*>(s_sq + jj * kSQS + 32);
                     float2 a2 = make_float2(0.0f, 0.0f);
 #pragma unroll
                     for (int g = 0; g < 8; ++g) {
-                        const float4 dd = P[3 * g], bb = P[3 * g + 1], ee = P[3 * g + 2];
                         a2 = scaled_group(make_float2(u8f(w[g], 0), u8f(w[g], 1)), make_float2(u8f(w[g], 2), u8f(w[g], 3)),
-                                          dd, bb, ee, a2);
+                                          D1[g], B1[g], E1[g], a2);
                     }
                     acc += a2.x + a2.y;
                     const bool alive = has && acc <= s_tsp[jj];
@@ -740,15 +765,22 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                     __syncwarp();
                     wcnt = rest;
                 };
+                // block 0's row terms x'' = c * delta', kept in registers for all the item's queries; eps'
+                // (the same for every query) is read from shared memory with the query's bases
+                float4 xd[8];
+#pragma unroll
+                for (int g = 0; g < 8; ++g) {
+                    const float4 d4 = reinterpret_cast<const float4*>(s_si)[g];
+                    const float2 x01 = __fmul2_rn(make_float2(cf[4 * g], cf[4 * g + 1]), make_float2(d4.x, d4.y));
+                    const float2 x23 = __fmul2_rn(make_float2(cf[4 * g + 2], cf[4 * g + 3]), make_float2(d4.z, d4.w));
+                    xd[g] = make_float4(x01.x, x01.y, x23.x, x23.y);
+                }
+                const float4* E0 = reinterpret_cast<const float4*>(s_si + 64);
                 for (int j = 0; j < n; ++j) {
-                    const float4* P = reinterpret_cast<const float4*>(s_sc + j * kSCS);
+                    const float4* Bq = reinterpret_cast<const float4*>(s_sq + j * kSQS);
                     float2 a2 = make_float2(0.0f, 0.0f);
 #pragma unroll
-                    for (int g = 0; g < 8; ++g) {
-                        const float4 dd = P[3 * g], bb = P[3 * g + 1], ee = P[3 * g + 2];
-                        a2 = scaled_group(make_float2(cf[4 * g], cf[4 * g + 1]), make_float2(cf[4 * g + 2], cf[4 * g + 3]),
-                                          dd, bb, ee, a2);
-                    }
+                    for (int g = 0; g < 8; ++g) a2 = scaled_group0(xd[g], Bq[g], E0[g], a2);
                     const float acc = a2.x + a2.y;
                     const bool alive = valid && acc <= s_tsp[j];
                     if (valid) {
@@ -979,7 +1011,7 @@ static size_t scan_smem(const trident_index& idx, int K, int G, bool lb) {
     if (lb) s += ((size_t)G * bws + 2 * (size_t)idx.num_blocks * kBS) * sizeof(float);  // base, delta, eps
     s += (size_t)G * KM * (sizeof(float) + sizeof(int32_t));                          // top-K lists
     s += qcap * (sizeof(uint32_t) + sizeof(float));                                   // survivors + distances
-    if (lb) s += (size_t)G * kSCS * sizeof(float);                                    // scaled intervals
+    if (lb) s += ((size_t)kSIS + (size_t)G * kSQS) * sizeof(float);                  // scaled intervals
     if (lb) s += (size_t)(T / 32) * kWB * (sizeof(float) + 2);                         // block-1 batches
     if (lb) s += (size_t)(T / 32) * kWQ * (sizeof(float) + sizeof(uint32_t) + 1);      // deep queues
     return s;
