@@ -1,26 +1,28 @@
 #!/usr/bin/env python3
 """Benchmark of the TRIDENT lossless IVF query path on B200: QPS at K=10.
 
-Workload (N = 1 GPU): configs[1] of the benchmark, "c2": N=1,000,000 rows, D=960, nlist=1024,
-nprobe=64, K=10, B=1000 queries; synthetic GIST1M-shaped rows (|N(0,1)| (d+1)^-0.7, unit sum),
-generated on the GPU from fixed seeds (the real dataset is not used). The cost router picks the
-cascade for this workload. With --gpus N the IVF lists are sharded across N ranks (one process
-per GPU) and every rank brings its own B queries. A step runs over the N * B queries:
+Default workload: "c4", the configuration on which the metric's 1/2/4/8-GPU scaling is
+quoted: N = 100,000,000 rows, D = 128, nlist = 65,536, nprobe = 256, K = 10, B = 10,000 queries in
+total; SIFT-shaped integer rows (a 4096-component Gaussian mixture, sigma 25, rounded and clipped to
+[0, 255]) generated on the GPU from fixed seeds (the real dataset is not used). It fits one B200
+(about 106 GB at the build's peak). With --gpus N the IVF lists are sharded across N ranks (one
+process per GPU) and the 10,000 queries are split between them (strong scaling):
   - each rank runs the coarse stage for its own queries; one NCCL all-gather shares the queries,
     rotated queries, side information and probe lists;
   - each rank seeds every query from its own lists; an all-gather of the seed lists and a device
     merge give each query's threshold;
-  - each rank scans its own lists;
+  - each rank scans its own lists for every query;
   - an all-to-all of the per-rank top-K lists and a device merge.
-Per-GPU work stays fixed, so the bench reports "weak" scaling.
+--config c1 | c2 | c3 run the other configurations; their B is per rank (weak scaling).
 
-One step = one search of the batch. `value` = N * B / step time with the queries already in HBM
-(device time by CUDA events per step, L2 flushed between steps, max over ranks). `e2e` = the same
-through the public API with the queries copied from pinned host memory and the results copied back
-inside the timed region. Every run checks a sample of queries against the CPU oracle first.
+One step = one search of the batch. `value` = all ranks' queries / step time with the queries already
+in HBM (device time by CUDA events per step, L2 flushed between steps, max over ranks). `e2e` = the
+same through the public API with the queries copied from pinned host memory and the results copied
+back inside the timed region. Every run checks a sample of queries against the CPU oracle first.
 
 `--impl reference` times the reference's own CPU exact IVF-Flat (omp_cpu_ivfflat_f32, built from
 the reference sources into oracle/_ref) with float64 probe selection, on the box's host cores.
+`--config c3 --sweep` times the cascade, CM-FP32 and the router over the c3 sweep.
 """
 import argparse
 import json
@@ -48,7 +50,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--config", default="c2")
+    p.add_argument("--config", default="c4")
     p.add_argument("--batch", type=int, default=0, help="queries per step (default: the config's B)")
     p.add_argument("--nprobe", type=int, default=0)
     p.add_argument("--k", type=int, default=0)
@@ -600,12 +602,26 @@ def run_ours(args, d: Dist):
     e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d.barrier()
     torch.cuda.synchronize()
-    e2e_start.record(copy)
-    with torch.cuda.stream(copy):
-        xq_bufs[0].copy_(xq_pin, non_blocking=True)
-        h2d_done[0].record(copy)
     last = None
-    for s in range(args.steps):
+    if d.world > 1:
+        # The staged multi-GPU step exchanges data between ranks inside every search, so each step runs
+        # its H2D copy, search and D2H copy in order on the compute stream (the copies are small
+        # against the step).
+        e2e_start.record(stream)
+        for s in range(args.steps):
+            cur = s & 1
+            xq_bufs[cur].copy_(xq_pin, non_blocking=True)
+            dd, ii = step(xq_bufs[cur])
+            out_h[cur][0].copy_(dd, non_blocking=True)
+            out_h[cur][1].copy_(ii, non_blocking=True)
+            last = cur
+        e2e_end.record(stream)
+    else:
+        e2e_start.record(copy)
+        with torch.cuda.stream(copy):
+            xq_bufs[0].copy_(xq_pin, non_blocking=True)
+            h2d_done[0].record(copy)
+    for s in range(args.steps if d.world == 1 else 0):
         cur = s & 1
         stream.wait_event(h2d_done[cur])
         if s >= 2:
@@ -626,7 +642,8 @@ def run_ours(args, d: Dist):
             out_h[cur][1].copy_(ii, non_blocking=True)
             d2h_done[cur].record(copy)
         last = cur
-    e2e_end.record(copy)
+    if d.world == 1:
+        e2e_end.record(copy)
     torch.cuda.synchronize()
     d.barrier()
     clk = clocks.stop()
@@ -677,9 +694,12 @@ def run_ours(args, d: Dist):
             "e2e": {"value": round(B * d.world / (e2e_ms / args.steps * 1e-3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": int(xq_pin.numel() * 4) * d.world,
                     "d2h_bytes_per_step": int(out_d_h.numel() * 4 + out_i_h.numel() * 8) * d.world,
-                    "method": "TridentV4Index.search per batch; H2D of the next batch and D2H of the previous "
-                              "results on a copy stream beside the search; timed from the first H2D to the last "
-                              "D2H (CUDA events), max over ranks; no L2 flush inside (index larger than L2)"},
+                    "method": ("TridentV4Index.search per batch; H2D of the next batch and D2H of the previous "
+                               "results on a copy stream beside the search; timed from the first H2D to the last "
+                               "D2H (CUDA events); no L2 flush inside (index larger than L2)") if d.world == 1 else
+                              ("ShardedSearch.search per batch: H2D of this rank's queries, the staged search, D2H "
+                               "of its merged results, in order on the compute stream; CUDA events around all "
+                               "steps, max over ranks; no L2 flush inside")},
             "gpu_launches": launches, "clocks": clk, "lossless_check": check,
             "roofline": roof, "cpu_baseline": cpu,
             **({"ooc": ooc} if ooc is not None else {}),
