@@ -63,6 +63,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-roofline", action="store_true")
     p.add_argument("--n", type=int, default=0, help="override N (rows) for quick runs")
+    p.add_argument("--nlist", type=int, default=0, help="override nlist")
+    p.add_argument("--n-comp", type=int, default=0, help="override the mixture's component count")
     p.add_argument("--sweep", action="store_true",
                    help="c3: time both modes and the router over B x nprobe x K, oracle-checking every cell")
     a = p.parse_args()
@@ -216,8 +218,12 @@ def workload_config(args):
         over["K"] = args.k
     if args.n:
         over["N"] = args.n
+    if args.nlist:
+        over["nlist"] = args.nlist
     if over:
         cfg = ds.scaled(cfg, **over)
+    if args.n_comp:
+        cfg = ds.Config(**{**cfg.__dict__, "n_comp": args.n_comp, "name": cfg.name.split("_")[0] + "_small"})
     return cfg
 
 
@@ -265,14 +271,25 @@ def make_workload(args, d: Dist):
     import torch
 
     from trident_b200 import SharedClusterStorage, TridentV4Index, choose_tile
-    from trident_b200.shard import partition_lists
+    from trident_b200.shard import list_work_estimate, partition_lists
 
     cfg = workload_config(args)
     t0 = time.perf_counter()
     xb, xq, lids, c_np, l_np, mu_np, R_np, strong = make_clustering(args, d, cfg)
     if d.world > 1:
+        # lists weighed by expected scan work: rows x (1 + probes among 8192 base rows used as
+        # stand-in queries), estimated on rank 0 and broadcast so every rank takes the same partition
         counts = np.bincount(l_np, minlength=cfg.nlist)
-        owner = torch.from_numpy(partition_lists(counts, d.world)).to(d.dev)
+        work = torch.zeros(cfg.nlist, dtype=torch.int64, device=d.dev)
+        if d.rank == 0:
+            g = torch.Generator(device="cpu")
+            g.manual_seed(ds_seed_balance())
+            samp = xb[torch.randperm(cfg.N, generator=g)[:8192].to(d.dev)].contiguous()
+            work.copy_(torch.from_numpy(list_work_estimate(samp, torch.from_numpy(c_np).to(d.dev), counts,
+                                                           cfg.nprobe)))
+            del samp
+        d.bcast(work)
+        owner = torch.from_numpy(partition_lists(work.cpu().numpy(), d.world)).to(d.dev)
         rows = torch.nonzero(owner[lids.long()] == d.rank).flatten()
         st = SharedClusterStorage(xb[rows], lids[rows], None, cfg.nlist, device=d.dev, host_rows=args.ooc)
         st.orig_ids_sorted = rows.to(torch.int32)[st.orig_ids_sorted.long()].contiguous()
@@ -289,6 +306,13 @@ def make_workload(args, d: Dist):
         f"in {time.perf_counter() - t0:.1f}s (index build {idx.build_s:.1f}s, peak device memory "
         f"{torch.cuda.max_memory_allocated(d.dev) / 1e9:.1f} GB)")
     return cfg, xq, c_np, l_np, idx, strong
+
+
+def ds_seed_balance() -> int:
+    """Seed of the base-row sample that estimates list work for the partition."""
+    from trident_b200 import datasets as ds
+
+    return ds.SEED_PCA + 100
 
 
 def host_storage(cfg, l_np, lists, device):
@@ -571,6 +595,10 @@ def run_ours(args, d: Dist):
     launches0 = int(_lib.lib().trident_launch_count())
     d.barrier()
     torch.cuda.synchronize()
+    # TRIDENT_PROFILE_REGION=1: the timed steps alone are the profiler's region (ncu --profile-from-start off)
+    region = bool(os.environ.get("TRIDENT_PROFILE_REGION"))
+    if region:
+        torch.cuda.profiler.start()
     for s in range(args.steps):
         flush.fill_(s & 0xFF)
         ph = {}
@@ -580,10 +608,20 @@ def run_ours(args, d: Dist):
         for n, v in ph.items():
             phase_tot[n] = phase_tot.get(n, 0.0) + v
     torch.cuda.synchronize()
+    if region:
+        torch.cuda.profiler.stop()
     d.barrier()
     launches = int(_lib.lib().trident_launch_count()) - launches0
     step_ms = [a.elapsed_time(b) for a, b in evs]
     total_ms = d.max(sum(step_ms))
+    scan_per_rank = [phase_tot.get("scan", 0.0) / args.steps]
+    if d.world > 1:  # every rank's scan time: the load balance of the list partition
+        import torch.distributed as dist
+
+        t = torch.tensor([scan_per_rank[0]], dtype=torch.float64, device=d.dev)
+        allt = torch.empty(d.world, dtype=torch.float64, device=d.dev)
+        dist.all_gather_into_tensor(allt, t)
+        scan_per_rank = [round(float(v), 4) for v in allt.cpu().tolist()]
     # ---- end to end through the public API: pinned host queries in, host results out. Serving
     # style: a copy stream moves batch s + 1 to the device and batch s - 1's results to the host
     # while batch s is searched (two device query buffers, events order the streams). The timed
@@ -689,6 +727,8 @@ def run_ours(args, d: Dist):
                       f"{idx.storage.xb_sorted.numel() * 4 / 1e9:.2f} GB FP32 rows",
                 "parallelism": f"list-sharded x{d.world}" if d.world > 1 else "single GPU",
                 "phase_ms_per_step": {n: round(v / args.steps, 4) for n, v in phase_tot.items()},
+                **({"scan_ms_per_rank": scan_per_rank,
+                    "partition": "lists weighed by rows x (1 + probes of 8192 base rows)"} if d.world > 1 else {}),
                 "step_ms_min_max": [round(min(step_ms), 4), round(max(step_ms), 4)],
             },
             "e2e": {"value": round(B * d.world / (e2e_ms / args.steps * 1e-3), 1), "unit": UNIT,

@@ -131,3 +131,25 @@ def test_partition_is_balanced_and_total():
         load = np.bincount(owner, weights=counts, minlength=R)
         assert load.sum() == counts.sum()
         assert load.max() - load.min() <= counts.max()  # greedy longest-first bound
+
+
+def test_list_work_estimate_and_balanced_partition():
+    """Work = rows x (1 + probes of the sample); the partition balances that work across ranks."""
+    import torch
+
+    from trident_b200.shard import list_work_estimate, partition_lists
+
+    rng = np.random.default_rng(4)
+    nlist, D, R = 64, 16, 4
+    cent = rng.standard_normal((nlist, D)).astype(np.float32) * 4
+    counts = rng.integers(1, 200, nlist)
+    # a sample concentrated near the first 8 centroids: those lists are probed far more often
+    hot = rng.integers(0, 8, 500)
+    sample = (cent[hot] + 0.1 * rng.standard_normal((500, D))).astype(np.float32)
+    work = list_work_estimate(torch.from_numpy(sample), torch.from_numpy(cent), counts, nprobe=2)
+    d = ((sample[:, None, :].astype(np.float64) - cent[None]) ** 2).sum(-1)
+    freq = np.bincount(np.argsort(d, axis=1, kind="stable")[:, :2].ravel(), minlength=nlist)
+    assert np.array_equal(work, counts * (freq + 1))
+    owner = partition_lists(work, R)
+    load = np.bincount(owner, weights=work, minlength=R)
+    assert load.max() <= load.mean() + work.max()  # greedy bound: within one list of the mean

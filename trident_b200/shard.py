@@ -1,6 +1,7 @@
 """Multi-GPU list sharding (one process per GPU; new relative to the single-GPU reference).
 
-The IVF lists are split across R ranks (greedy longest-first on list length, ties by list id).
+The IVF lists are split across R ranks (greedy largest-first onto the least-loaded rank, ties by list
+id), weighing each list by its length or, better, by its expected scan work (list_work_estimate).
 Every rank holds ALL centroids, mean64 and R64 but only the rows of its own lists: lists owned by
 other ranks are empty in its index. Each rank brings its own B queries; a step over the R * B
 queries of all ranks runs the staged search:
@@ -34,6 +35,27 @@ def partition_lists(counts, R: int) -> np.ndarray:
         owner[c] = r
         load[r] += counts[c]
     return owner
+
+
+def list_work_estimate(sample, centroids, counts, nprobe: int, chunk: int = 4096) -> np.ndarray:
+    """Expected scan work of each list, for balancing the partition: rows x (1 + how many of the
+    `sample` rows probe the list among their nprobe nearest centroids). A list's scan cost grows with
+    the queries that probe it, not only with its length; rows of the dataset stand in for queries
+    (they come from the same distribution). `sample` and `centroids` are float32 tensors on one
+    device (float32 products: only the counts matter). Returns int64 [nlist]."""
+    import torch
+
+    nlist = int(centroids.shape[0])
+    cn = (centroids.double() ** 2).sum(1).float()
+    freq = torch.zeros(nlist, dtype=torch.int64, device=sample.device)
+    ct = centroids.t().contiguous()
+    k = min(int(nprobe), nlist)
+    for s in range(0, int(sample.shape[0]), chunk):
+        d = torch.addmm(cn.unsqueeze(0), sample[s:s + chunk], ct, beta=1.0, alpha=-2.0)
+        idx = torch.topk(d, k, dim=1, largest=False).indices
+        freq += torch.bincount(idx.flatten(), minlength=nlist)
+    counts = torch.as_tensor(np.asarray(counts, np.int64), device=sample.device)
+    return (counts * (freq + 1)).cpu().numpy()
 
 
 def shard_rows(list_ids, owner, rank: int) -> np.ndarray:
