@@ -4,9 +4,9 @@ probe_select_kernel has three ways to find the nprobe-th approximate coarse valu
 float64 re-check of the boundary:
   * nlist <= 1024: each thread's keys in registers (c1, c2; covered by test_gpu_search);
   * nlist <= 8192: the query's row cached in shared memory (c3: nlist 4096);
-  * above that: an upper bound from the coarse GEMM's per-tile row minima, then one pass over the row
-    (c4: nlist 65,536; c5: 262,144), or, when nprobe exceeds the number of 128-list tiles, an exact
-    per-bit search that re-reads the row.
+  * above that: an upper bound from the coarse GEMM's row minima over 64-list spans, then one pass
+    over the row (c4: nlist 65,536; c5: 262,144), or, when nprobe exceeds the number of spans, an
+    exact per-bit search that re-reads the row.
 Each case checks the probe lists and their float64 distances bit for bit against the oracle
 (oracle_probe_select_f64: the nprobe smallest float64 ||q - c||^2, ties to the smaller list id), and
 the search's top-K (ids identical, distances bit-identical) against the oracle's exact IVF-Flat.
@@ -90,11 +90,11 @@ def test_probe_sets_and_topk_at_config_list_counts(cfg_name, over, centroids, mo
         assert_same_topk(d, i, od, oi)
 
 
-def test_probe_sets_when_nprobe_exceeds_the_tile_count():
-    """16,384 lists are 128 GEMM tiles; nprobe = 256 cannot be bounded by the per-tile minima, so the
-    exact per-bit search over the row in global memory runs."""
+def test_probe_sets_when_nprobe_exceeds_the_span_count():
+    """16,384 lists give 256 row minima over 64-list spans; nprobe = 300 cannot be bounded by them, so
+    the exact per-bit search over the row in global memory runs."""
     from trident_b200 import datasets as ds
 
-    cfg = ds.scaled(ds.CONFIGS["c4"], N=200_000, nlist=16_384, nprobe=256, B=300, K=10)
+    cfg = ds.scaled(ds.CONFIGS["c4"], N=200_000, nlist=16_384, nprobe=300, B=300, K=10)
     _, xq, cent, _, idx = _build(cfg, "rows")
     _coarse_matches_oracle(idx, xq, cent, cfg.nprobe)

@@ -86,7 +86,7 @@ size_t carve_workspace(const trident_index& idx, int B, int K, int nprobe, void*
     w.qrot = (float*)take(Bs * idx.D_pad * sizeof(float));
     w.qinfo = (float*)take(Bs * QI_LEN * sizeof(float));
     w.coarse = (float*)take(Bs * (size_t)idx.nlist * sizeof(float));
-    w.tilemin = (float*)take(Bs * (size_t)((idx.nlist + kCoarseTileN - 1) / kCoarseTileN) * sizeof(float));
+    w.tilemin = (float*)take(Bs * (size_t)((idx.nlist + kCoarseMinSpan - 1) / kCoarseMinSpan) * sizeof(float));
     w.gsplit = (float*)take(coarse_split_bytes(idx, (int)Bs));
     w.probe = (int32_t*)take(pairs * sizeof(int32_t));
     w.cnt = (int32_t*)take(2 * (size_t)idx.nlist * sizeof(int32_t));

@@ -193,7 +193,7 @@ constexpr int kSelNW = kSelThreads / 32;
 constexpr int kSelCap = 2048;        // sorted best (<= nprobe <= 1024) + one batch of re-check members
 constexpr int kSelSmemKeys = 8192;
 constexpr int kSelRegKeys = 4;      // keys per thread held in registers by the threshold search (nlist <= 1024)
-constexpr int kSelTileKeys = 8;     // per-tile minima per thread (up to 2048 tiles of kCoarseTileN lists)
+constexpr int kSelTileKeys = 16;    // span minima per thread (up to 4096 spans of kCoarseMinSpan lists)
 
 __device__ void bitonic_sort_kc(unsigned long long* key, int32_t* cid, int P) {
     for (int k = 2; k <= P; k <<= 1) {
@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
 
     // 1) t >= the nprobe-th smallest approximate value (equal to it except on the tile-minimum path)
     uint32_t ans = 0;
-    const int ntiles = (nlist + kCoarseTileN - 1) / kCoarseTileN;
+    const int ntiles = (nlist + kCoarseMinSpan - 1) / kCoarseMinSpan;  // entries of the row-minimum array
     if (nlist <= kSelRegKeys * kSelThreads) {  // exact, this thread's keys in registers
         uint32_t kr[kSelRegKeys];
 #pragma unroll
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(kSelThreads, 4) probe_select_kernel(
         }
         ans = kth_smallest_key<kSelRegKeys>(kr, nlist, nprobe, red);
     } else if (!cached && tilemin && nprobe <= ntiles && ntiles <= kSelTileKeys * kSelThreads) {
-        // An upper bound from the GEMM's per-tile minima: the nprobe smallest of them are nprobe
+        // An upper bound from the GEMM's row minima over 64-list spans: the nprobe smallest of them are nprobe
         // distinct entries of the row, so the row's nprobe-th smallest value is <= their largest.
         // The member pass below then reads the row once instead of once per bit.
         uint32_t kr[kSelTileKeys];

@@ -16,10 +16,10 @@
 //               (12 per slice for 3xTF32: hi*hi + hi*lo + lo*hi; 4 for 1xTF32) into one of two
 //               tensor-memory accumulators and commits the stage back to the producer; after the
 //               tile's last slice it commits the accumulator to the epilogue.
-//   warps 2-5   epilogue: each thread owns one accumulator row (tensor-memory lane), reads the
-//               tile's 128 columns with tcgen05.ld and writes distances (and the tile minimum) or
-//               keeps a running argmin, then frees the accumulator, so the next tile's MMAs
-//               overlap this epilogue.
+//   epilogue    each thread owns one accumulator row (tensor-memory lane): eight warps of 64
+//               columns write distances and each row's minimum over its 64 lists (two warps per lane
+//               quarter), or four warps of 128 columns keep a running argmin. They read the
+//               accumulator with tcgen05.ld and free it, so the next tile's MMAs overlap them.
 // Shared memory holds three stages (64 KB each for 3xTF32). Every wait is bounded: a wait that
 // gives up (or sees another warp give up) sets the status word, the producer then waits (bounded)
 // for the copies it issued, the MMA warp for its last commit, and the tensor memory is freed.
@@ -47,12 +47,20 @@ constexpr int kGM = 128;                 // rows of A per tile (UMMA M)
 constexpr int kGN = kCoarseTileN;        // rows of B per tile (UMMA N)
 constexpr int kGK = 32;                  // K per stage
 constexpr int kGStages = 3;
-constexpr int kGThreads = 192;           // producer, MMA issuer, four epilogue warps
+// producer, MMA issuer, then the epilogue: four warps of 128 columns (argmin: each row's minimum stays
+// in one thread) or eight of 64 (distances: two warps per tensor-memory lane quarter)
+template <bool ARGMIN>
+struct EpiShape {
+    static constexpr int kWarps = ARGMIN ? 4 : 8;
+    static constexpr int kCols = kCoarseTileN * 4 / kWarps;
+    static constexpr int kThreads = 64 + 32 * kWarps;
+};
 constexpr int kGOpBytes = kGM * kGK * 4; // one operand split of one stage: 16 KB
 constexpr uint32_t kGTmemCols = 2 * kGN; // two accumulators of 128 columns
 constexpr uint32_t kGDrainPolls = 1u << 22;
 
 static_assert(kGM == kGN, "square tiles: A and B stage buffers have the same size");
+static_assert(EpiShape<false>::kCols == kCoarseMinSpan, "one row minimum per epilogue warp and tile");
 
 template <int SPLITS>
 struct GemmShape {
@@ -144,11 +152,12 @@ __device__ __forceinline__ void tma_slice(void* dst, const CUtensorMap* map, int
 struct GemmParams {
     int M, N, KT;           // rows of A, rows of B, K slices of 32
     int n_tiles, n_split;   // B tiles, B-tile ranges per A block (units = m_blocks * n_split)
+    int n_min;              // entries per row of the row-minimum array: ceil(N / kCoarseMinSpan)
     int units;
     uint32_t polls;
     const float* cn;        // [N] ||c||^2
     float* out;             // coarse: [M, N] distances
-    float* tilemin;         // coarse: [M, n_tiles] (optional)
+    float* tilemin;         // coarse: [M, n_min] minima over 64-column spans (optional)
     int32_t* arg_out;       // assignment: [M] nearest row of B
     int32_t* err;
 };
@@ -163,7 +172,7 @@ __device__ __forceinline__ void unit_range(const GemmParams& p, int u, int& m, i
 }
 
 template <int SPLITS, bool ARGMIN>
-__global__ void __launch_bounds__(kGThreads, 1)
+__global__ void __launch_bounds__(EpiShape<ARGMIN>::kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap mA_hi, const __grid_constant__ CUtensorMap mA_lo,
                    const __grid_constant__ CUtensorMap mB_hi, const __grid_constant__ CUtensorMap mB_lo,
                    const GemmParams p) {
@@ -172,7 +181,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
     __shared__ __align__(8) uint64_t full[kGStages], empty[kGStages], tfull[2], tempty[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
-    __shared__ float s_cn[4][kGN];  // per epilogue warp: the current tile's ||c||^2
+    using E = EpiShape<ARGMIN>;
+    __shared__ float s_cn[E::kWarps][E::kCols];  // per epilogue warp: its columns' ||c||^2
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(g_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -190,7 +200,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             gbar_init(&tfull[b], 1);
-            gbar_init(&tempty[b], 4);
+            gbar_init(&tempty[b], E::kWarps);
         }
         s_abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -310,8 +320,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
     } else {
         // ---------------- epilogue: thread = accumulator row
-        const int quarter = warp & 3;  // tensor-memory lanes 32 * quarter ... (warps 2-5 cover 0-3)
-        float* cnw = s_cn[warp - 2];   // this warp's copy of the tile's norms (no cross-warp barrier)
+        const int quarter = warp & 3;      // tensor-memory lanes 32 * quarter ... (each run of 4 warps covers 0-3)
+        const int half = (warp - 2) >> 2;  // which 64-column half (eight epilogue warps; 0 with four)
+        const int cbeg = half * E::kCols;  // this warp's first column of the tile
+        float* cnw = s_cn[warp - 2];       // this warp's copy of its columns' norms (no cross-warp barrier)
         const bool vec = !ARGMIN && ((p.N & 3) == 0) && ((((uintptr_t)p.out) | ((uintptr_t)p.cn)) & 15) == 0;
         uint32_t tile_iter = 0;
         bool ok = true;
@@ -324,11 +336,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
             for (int n = lo; n < hi; ++n, ++tile_iter) {
                 const int buf = tile_iter & 1;
                 const uint32_t tpar = (tile_iter >> 1) & 1u;
-                const int col_base = n * kGN;
-                // the tile's norms: issued before the wait, so their latency overlaps it
-                float cnv[kGN / 32];
+                const int col_base = n * kGN + cbeg;
+                // this warp's norms: issued before the wait, so their latency overlaps it
+                float cnv[E::kCols / 32];
 #pragma unroll
-                for (int i = 0; i < kGN / 32; ++i) {
+                for (int i = 0; i < E::kCols / 32; ++i) {
                     const int col = col_base + i * 32 + lane;
                     cnv[i] = col < p.N ? __ldg(p.cn + col) : 0.0f;
                 }
@@ -339,14 +351,15 @@ __global__ void __launch_bounds__(kGThreads, 1)
                     break;
                 }
 #pragma unroll
-                for (int i = 0; i < kGN / 32; ++i) cnw[i * 32 + lane] = cnv[i];
+                for (int i = 0; i < E::kCols / 32; ++i) cnw[i * 32 + lane] = cnv[i];
                 __syncwarp();
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * kGN);
+                const uint32_t taddr =
+                    tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(buf * kGN) + (uint32_t)cbeg;
                 float rmin = kInf;
                 float* dst = (!ARGMIN && row < p.M) ? p.out + (int64_t)row * p.N + col_base : nullptr;
 #pragma unroll 1
-                for (int c0 = 0; c0 < kGN; c0 += 32) {
+                for (int c0 = 0; c0 < E::kCols; c0 += 32) {
                     uint32_t r[32];
                     asm volatile(
                         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
@@ -379,7 +392,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
                             o.z = cnw[c0 + 4 * v + 2] - 2.0f * __uint_as_float(r[4 * v + 2]);
                             o.w = cnw[c0 + 4 * v + 3] - 2.0f * __uint_as_float(r[4 * v + 3]);
                             rmin = fminf(rmin, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
-                            reinterpret_cast<float4*>(dst + c0)[v] = o;
+                            // streaming store: the distances must not evict the operands from L2
+                            __stcs(reinterpret_cast<float4*>(dst + c0) + v, o);
                         }
                     } else {
 #pragma unroll
@@ -387,7 +401,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
                             if (col0 + j < p.N) {
                                 const float o = cnw[c0 + j] - 2.0f * __uint_as_float(r[j]);
                                 rmin = fminf(rmin, o);
-                                dst[c0 + j] = o;
+                                __stcs(dst + c0 + j, o);
                             }
                         }
                     }
@@ -396,7 +410,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) gbar_arrive(&tempty[buf]);
-                if (!ARGMIN && p.tilemin && row < p.M) p.tilemin[(int64_t)row * p.n_tiles + n] = rmin;
+                if (!ARGMIN && p.tilemin && row < p.M) {
+                    const int span = n * (kGN / kCoarseMinSpan) + half;  // E::kCols == kCoarseMinSpan here
+                    if (span < p.n_min) __stcs(p.tilemin + (int64_t)row * p.n_min + span, rmin);
+                }
             }
             if (ARGMIN && ok && row < p.M) p.arg_out[row] = best_i;
         }
@@ -474,7 +491,7 @@ cudaError_t launch_gemm(const CUtensorMap* maps, GemmParams p, cudaStream_t st) 
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kSmem);
     if (e != cudaSuccess) return e;
     const int grid = p.units < num_sms() ? p.units : num_sms();
-    kern<<<grid, kGThreads, S::kSmem, st>>>(maps[0], maps[SPLITS == 3 ? 1 : 0], maps[SPLITS == 3 ? 2 : 1],
+    kern<<<grid, EpiShape<ARGMIN>::kThreads, S::kSmem, st>>>(maps[0], maps[SPLITS == 3 ? 1 : 0], maps[SPLITS == 3 ? 2 : 1],
                                             maps[SPLITS == 3 ? 3 : 1], p);
     return cudaGetLastError();
 }
@@ -506,6 +523,7 @@ cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B,
     p.N = idx.nlist;
     p.KT = Dp / kGK;
     p.n_tiles = (idx.nlist + kGN - 1) / kGN;
+    p.n_min = (idx.nlist + kCoarseMinSpan - 1) / kCoarseMinSpan;
     const int m_blocks = (B + kGM - 1) / kGM;
     // enough units for two per SM, each a contiguous range of B tiles of one A block
     int ns = (2 * num_sms() + m_blocks - 1) / m_blocks;

@@ -15,8 +15,9 @@ enum QInfo { QI_QNORM = 0, QI_SIGMA = 1, QI_CNORM = 2, QI_PAD = 3, QI_LEN = 4 };
 
 // Word of the counter block that holds the search's device-side status (TRIDENT_STATUS_*).
 constexpr int kStatusWord = 15;
-// Lists per tile of the coarse GEMM (and per entry of its per-tile row minima).
+// Lists per tile of the coarse GEMM, and per entry of its row minima (two entries per tile).
 constexpr int kCoarseTileN = 128;
+constexpr int kCoarseMinSpan = 64;
 
 // Workspace carve-up for one call (B, K, nprobe); every region is 256-byte aligned. The counter
 // block comes first, so the status word sits at the same offset whatever B, K and nprobe are.
@@ -24,7 +25,7 @@ struct Workspace {
     float* qrot;        // [B, D_pad]
     float* qinfo;       // [B, QI_LEN]
     float* coarse;      // [B, nlist] approximate ||c||^2 - 2 q.c
-    float* tilemin;     // [B, ceil(nlist / kCoarseTileN)] minimum of each row over each GEMM tile
+    float* tilemin;     // [B, ceil(nlist / kCoarseMinSpan)] minimum of each row over each 64-list span
     float* gsplit;      // coarse_split_bytes(idx, B): TF32 hi/lo splits of queries and centroids
     int32_t* probe;     // [B, nprobe]
     int32_t* cnt;       // [2, nlist]
@@ -58,8 +59,8 @@ cudaError_t launch_rotate_f64(const trident_index& idx, const float* xq, int B, 
 cudaError_t launch_rotate(const trident_index& idx, const float* xq, int B, float* qrot, float* qinfo,
                           uint32_t* tau, cudaStream_t st);
 // Persistent TMA-fed tcgen05 GEMM (tb_gemm.cu), 3xTF32; sets *err |= TRIDENT_STATUS_MMA_TIMEOUT if a
-// bounded wait gave up. tilemin (optional, [B, ceil(nlist / kCoarseTileN)]) receives each row's
-// minimum over each tile; splits is scratch of coarse_split_bytes(idx, B) bytes for the operands'
+// bounded wait gave up. tilemin (optional, [B, ceil(nlist / kCoarseMinSpan)]) receives each row's
+// minimum over each 64-list span; splits is scratch of coarse_split_bytes(idx, B) bytes for the operands'
 // TF32 hi/lo splits.
 size_t coarse_split_bytes(const trident_index& idx, int B);
 cudaError_t launch_coarse_gemm(const trident_index& idx, const float* xq, int B, float* coarse, float* tilemin,
