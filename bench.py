@@ -622,30 +622,22 @@ def run_ours(args, d: Dist):
         allt = torch.empty(d.world, dtype=torch.float64, device=d.dev)
         dist.all_gather_into_tensor(allt, t)
         scan_per_rank = [round(float(v), 4) for v in allt.cpu().tolist()]
-    # ---- end to end through the public API: pinned host queries in, host results out. Serving
-    # style: a copy stream moves batch s + 1 to the device and batch s - 1's results to the host
-    # while batch s is searched (two device query buffers, events order the streams). The timed
-    # region runs from the first H2D to the last D2H, covering every step's copies. There is no L2
-    # flush inside it; the index (codes + rows) is larger than L2.
-    out_h = [(torch.empty((B, K), dtype=torch.float32, pin_memory=True),
-              torch.empty((B, K), dtype=torch.int64, pin_memory=True)) for _ in range(2)]
-    out_d_h, out_i_h = out_h[0]
-    xq_bufs = [torch.empty_like(xq_dev), torch.empty_like(xq_dev)]
-    out_bufs = [(torch.empty((B, K), dtype=torch.float32, device=d.dev),
-                 torch.empty((B, K), dtype=torch.int64, device=d.dev)) for _ in range(2)]
-    copy = torch.cuda.Stream(device=d.dev)
-    h2d_done = [torch.cuda.Event() for _ in range(2)]
-    search_done = [torch.cuda.Event() for _ in range(2)]
-    d2h_done = [torch.cuda.Event() for _ in range(2)]
-    e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # ---- end to end through the public API: pinned host queries in, host results out.
+    #  * one GPU: TridentV4Index.search_stream over the steps' queries in sub-batches of B (a copy
+    #    stream uploads the next sub-batch and downloads the previous results while the current one is
+    #    searched), timed by its CUDA events from the first upload to the last download;
+    #  * several GPUs: the staged search exchanges data between ranks inside every step, so each step
+    #    runs its H2D copy, search and D2H copy in order on the compute stream.
+    # There is no L2 flush inside; the index (codes + rows) is larger than L2.
     d.barrier()
     torch.cuda.synchronize()
-    last = None
     if d.world > 1:
-        # The staged multi-GPU step exchanges data between ranks inside every search, so each step runs
-        # its H2D copy, search and D2H copy in order on the compute stream (the copies are small
-        # against the step).
+        out_h = [(torch.empty((B, K), dtype=torch.float32, pin_memory=True),
+                  torch.empty((B, K), dtype=torch.int64, pin_memory=True)) for _ in range(2)]
+        xq_bufs = [torch.empty_like(xq_dev), torch.empty_like(xq_dev)]
+        e2e_start, e2e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e2e_start.record(stream)
+        last = 0
         for s in range(args.steps):
             cur = s & 1
             xq_bufs[cur].copy_(xq_pin, non_blocking=True)
@@ -654,39 +646,18 @@ def run_ours(args, d: Dist):
             out_h[cur][1].copy_(ii, non_blocking=True)
             last = cur
         e2e_end.record(stream)
+        torch.cuda.synchronize()
+        e2e_local = e2e_start.elapsed_time(e2e_end)
+        out_d_h, out_i_h = out_h[last]
     else:
-        e2e_start.record(copy)
-        with torch.cuda.stream(copy):
-            xq_bufs[0].copy_(xq_pin, non_blocking=True)
-            h2d_done[0].record(copy)
-    for s in range(args.steps if d.world == 1 else 0):
-        cur = s & 1
-        stream.wait_event(h2d_done[cur])
-        if s >= 2:
-            stream.wait_event(d2h_done[cur])  # out_bufs[cur] still being copied out from step s - 2
-        dd, ii = step(xq_bufs[cur], out=out_bufs[cur])
-        dd.record_stream(copy)  # the copy stream reads them
-        ii.record_stream(copy)
-        search_done[cur].record(stream)
-        with torch.cuda.stream(copy):
-            if s + 1 < args.steps:  # the next batch's queries, into the other buffer once it is free
-                copy.wait_event(search_done[cur ^ 1]) if s >= 1 else None
-                xq_bufs[cur ^ 1].copy_(xq_pin, non_blocking=True)
-                h2d_done[cur ^ 1].record(copy)
-            copy.wait_event(search_done[cur])
-            if s >= 2:
-                copy.wait_event(d2h_done[cur])
-            out_h[cur][0].copy_(dd, non_blocking=True)
-            out_h[cur][1].copy_(ii, non_blocking=True)
-            d2h_done[cur].record(copy)
-        last = cur
-    if d.world == 1:
-        e2e_end.record(copy)
-    torch.cuda.synchronize()
+        xq_steps = xq_pin.repeat(args.steps, 1).pin_memory()
+        tm = {}
+        sd, si = idx.search_stream(xq_steps, nprobe, k=K, batch=B, mode=mode, ub_seed=args.ub_seed, timing=tm)
+        e2e_local = tm["ms"]
+        out_d_h, out_i_h = sd[-B:], si[-B:]
     d.barrier()
     clk = clocks.stop()
-    e2e_ms = d.max(e2e_start.elapsed_time(e2e_end))
-    out_d_h, out_i_h = out_h[last]
+    e2e_ms = d.max(e2e_local)
     assert np.array_equal(out_i_h.numpy(), got_i)
 
     result = None
@@ -734,9 +705,10 @@ def run_ours(args, d: Dist):
             "e2e": {"value": round(B * d.world / (e2e_ms / args.steps * 1e-3), 1), "unit": UNIT,
                     "h2d_bytes_per_step": int(xq_pin.numel() * 4) * d.world,
                     "d2h_bytes_per_step": int(out_d_h.numel() * 4 + out_i_h.numel() * 8) * d.world,
-                    "method": ("TridentV4Index.search per batch; H2D of the next batch and D2H of the previous "
-                               "results on a copy stream beside the search; timed from the first H2D to the last "
-                               "D2H (CUDA events); no L2 flush inside (index larger than L2)") if d.world == 1 else
+                    "method": ("TridentV4Index.search_stream over the steps' queries in sub-batches of B: H2D "
+                               "of the next sub-batch and D2H of the previous results on a copy stream beside the "
+                               "search; its CUDA events from the first H2D to the last D2H; no L2 flush inside "
+                               "(index larger than L2)") if d.world == 1 else
                               ("ShardedSearch.search per batch: H2D of this rank's queries, the staged search, D2H "
                                "of its merged results, in order on the compute stream; CUDA events around all "
                                "steps, max over ranks; no L2 flush inside")},

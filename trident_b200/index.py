@@ -222,12 +222,48 @@ class TridentV4Index:
         # of the exact distance (4 ceil(D/128) chained fma + 5 tree adds + the subtraction).
         self.lb_rel_slack = float((D_pad + 4 * math.ceil(D / 128) + 32) * U32 * 1.01)
         self.build_s = time.perf_counter() - t0
+        self._reset_runtime()
 
+    def _reset_runtime(self):
+        """Per-index state of the search calls (descriptor, workspace, output buffers)."""
         self._desc = None
         self._ws = None
         self._ws_key = None
         self._out = {}
         self._stats_tmp = None
+
+    @classmethod
+    def from_arrays(cls, storage: SharedClusterStorage, arrays: dict, params: dict, device="cuda:0",
+                    max_batch: int = 1024, max_nprobe: int = 512, max_k: int = 100):
+        """An index from already-built arrays (trident_b200.artifacts.load_index), without the SQ8
+        build. `arrays` holds device tensors: centroids, centroid_norm_sq, codes, vmin, delta, eps,
+        tile_off, pca_mean, pca_rot; `params` the scalars tile_size, per_cluster_sq8, use_pca,
+        centroid_norm_max, lb_rel_slack, total_tiles, plus mean64 and R64 (NumPy float64)."""
+        torch = _torch()
+        self = cls.__new__(cls)
+        self.storage = storage
+        self.dev = torch.device(device)
+        self.N, self.D, self.nlist = storage.N, storage.D, storage.nlist
+        self.tile_size = int(params["tile_size"])
+        self.per_cluster_sq8 = int(params["per_cluster_sq8"])
+        self.use_pca = int(params["use_pca"])
+        self.var_block = 0
+        self.D_pad = ((self.D + 31) // 32) * 32
+        self.num_blocks = self.D_pad // 32
+        self.max_batch, self.max_nprobe, self.max_k = int(max_batch), int(max_nprobe), int(max_k)
+        self.mean64, self.R64 = params["mean64"], params["R64"]
+        self.centroids = arrays["centroids"]
+        self.centroid_norm_sq = arrays["centroid_norm_sq"]
+        self.centroid_norm_max = float(params["centroid_norm_max"])
+        self.codes = arrays["codes"]
+        self.vmin_pad, self.delta_pad, self.eps_pad = arrays["vmin"], arrays["delta"], arrays["eps"]
+        self.cluster_tile_off = arrays["tile_off"]
+        self.total_tiles = int(params["total_tiles"])
+        self.pca_mean, self.pca_rot = arrays["pca_mean"], arrays["pca_rot"]
+        self.lb_rel_slack = float(params["lb_rel_slack"])
+        self.build_s = 0.0
+        self._reset_runtime()
+        return self
 
     # ------------------------------------------------------------------------------------------
     def desc(self) -> _lib.TridentIndexDesc:
@@ -361,6 +397,74 @@ class TridentV4Index:
             ev1.synchronize()
             ms = ev0.elapsed_time(ev1)
         return topk_d, topk_i, ms
+
+    def search_stream(self, xq_host, nprobe: int, k: int = 10, batch: Optional[int] = None, mode: int = -1,
+                      ub_seed: int = 0, timing: Optional[dict] = None):
+        """Top-k of many host queries, streamed through the search in sub-batches of `batch` (default
+        max_batch): a copy stream uploads sub-batch s + 1 into the second of two device buffers and
+        downloads sub-batch s - 1's results into pinned host memory while sub-batch s is searched
+        (events order the streams). mode = -1 routes each sub-batch on its own size. Returns pinned
+        host tensors (distances [Q, k] float32, ids [Q, k] int64). timing (a dict) receives 'ms': CUDA
+        events from before the first upload to after the last download.
+
+        Caller-side streaming of the reference's drivers, which copy each batch and call search on it
+        (benchmarks/phase4a_suite.py:280-342), moved into the index."""
+        torch = _torch()
+        x = xq_host if isinstance(xq_host, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(xq_host, np.float32))
+        if x.is_cuda or x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != self.D:
+            raise ValueError(f"xq_host must be a float32 host array [Q, {self.D}]")
+        x = x.contiguous()
+        if not x.is_pinned():
+            x = x.pin_memory()
+        Q, K = int(x.shape[0]), int(k)
+        bs = int(batch or self.max_batch)
+        out_d = torch.empty((Q, K), dtype=torch.float32, pin_memory=True)
+        out_i = torch.empty((Q, K), dtype=torch.int64, pin_memory=True)
+        if Q == 0:
+            return out_d, out_i
+        comp = torch.cuda.current_stream(self.dev)
+        copy = getattr(self, "_copy_stream", None)
+        if copy is None:
+            copy = self._copy_stream = torch.cuda.Stream(device=self.dev)
+        qbuf = [torch.empty((bs, self.D), dtype=torch.float32, device=self.dev) for _ in range(2)]
+        rbuf = [(torch.empty((bs, K), dtype=torch.float32, device=self.dev),
+                 torch.empty((bs, K), dtype=torch.int64, device=self.dev)) for _ in range(2)]
+        ev = lambda t=False: torch.cuda.Event(enable_timing=t)
+        h2d, done, d2h = [ev(), ev()], [ev(), ev()], [ev(), ev()]
+        t0, t1 = ev(True), ev(True)
+        nb = (Q + bs - 1) // bs
+        t0.record(copy)
+        with torch.cuda.stream(copy):
+            b0 = min(bs, Q)
+            qbuf[0][:b0].copy_(x[:b0], non_blocking=True)
+            h2d[0].record(copy)
+        for s in range(nb):
+            cur, lo = s & 1, s * bs
+            b = min(bs, Q - lo)
+            comp.wait_event(h2d[cur])
+            if s >= 2:
+                comp.wait_event(d2h[cur])  # rbuf[cur] of sub-batch s - 2 is on its way to the host
+            m = self.route(b, nprobe) if mode == -1 else mode
+            self.search(qbuf[cur][:b], nprobe, mode=m, k=K, ub_seed=ub_seed,
+                        out=(rbuf[cur][0][:b], rbuf[cur][1][:b]))
+            done[cur].record(comp)
+            with torch.cuda.stream(copy):
+                if s + 1 < nb:  # the next sub-batch, once search s - 1 has released its buffer
+                    if s >= 1:
+                        copy.wait_event(done[cur ^ 1])
+                    nlo = lo + bs
+                    b2 = min(bs, Q - nlo)
+                    qbuf[cur ^ 1][:b2].copy_(x[nlo:nlo + b2], non_blocking=True)
+                    h2d[cur ^ 1].record(copy)
+                copy.wait_event(done[cur])
+                out_d[lo:lo + b].copy_(rbuf[cur][0][:b], non_blocking=True)
+                out_i[lo:lo + b].copy_(rbuf[cur][1][:b], non_blocking=True)
+                d2h[cur].record(copy)
+        t1.record(copy)
+        t1.synchronize()
+        if timing is not None:
+            timing["ms"] = t0.elapsed_time(t1)
+        return out_d, out_i
 
     # ---- the search in three stages, for list sharding over GPUs (trident_b200.shard)
     def search_prep(self, xq_gpu, nprobe: int):
