@@ -129,7 +129,7 @@ class ShardedSearch:
         dist.all_gather_into_tensor(out, t.contiguous(), group=self.group)
         return out
 
-    def search(self, xq, nprobe: int, k: int = 10, mode: int = 2, ub_seed: int = 0, phase_ms=None):
+    def search(self, xq, nprobe: int, k: int = 10, mode: int = 2, ub_seed: int = 0, phase_ms=None, stats_buf=None):
         import torch
         import torch.distributed as dist
 
@@ -161,7 +161,8 @@ class ShardedSearch:
         sd_all, si_all = self._unpack(self._gather(self._pack(seed_d, seed_i)), R, R * B, k)
         tau = self._merge(sd_all, si_all)[0][:, k - 1].contiguous()
         mark("scan")
-        d_loc, i_loc = self.index.search_finish(xq_all, tau, nprobe, k=k, mode=mode, ub_seed=ub_seed)
+        kw = {} if stats_buf is None else {"stats_buf": stats_buf}  # counters of this rank's scan
+        d_loc, i_loc = self.index.search_finish(xq_all, tau, nprobe, k=k, mode=mode, ub_seed=ub_seed, **kw)
         mark("exchange")
         # rank-major chunks of B queries: rank r receives chunk r of every rank -> [R, B, k]
         loc = self._pack(d_loc, i_loc)
