@@ -783,10 +783,6 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                     for (int g = 0; g < 8; ++g) a2 = scaled_group0(xd[g], Bq[g], E0[g], a2);
                     const float acc = a2.x + a2.y;
                     const bool alive = valid && acc <= s_tsp[j];
-                    if (valid) {
-                        st_cand += 1;
-                        st_dims += 32u;
-                    }
                     const unsigned m = __ballot_sync(TB_FULL, alive);
                     if (!m) continue;
                     if (nb == 1) {
@@ -810,6 +806,10 @@ __global__ void __launch_bounds__(T, kScanThreadsPerSm / T) scan_kernel(const Sc
                         run_batch(32);
                         while (wq_n >= 32) deep_round(0);
                     }
+                }
+                if (valid) {  // block 0 of this row for every query of the item
+                    st_cand += (unsigned)n;
+                    st_dims += 32u * (unsigned)n;
                 }
                 // the chunk's block-1 codes leave the registers: finish this warp's batch
                 if (wcnt > 0) run_batch(wcnt);
