@@ -23,6 +23,8 @@ back inside the timed region. Every run checks a sample of queries against the C
 `--impl reference` times the reference's own CPU exact IVF-Flat (omp_cpu_ivfflat_f32, built from
 the reference sources into oracle/_ref) with float64 probe selection, on the box's host cores.
 `--config c3 --sweep` times the cascade, CM-FP32 and the router over the c3 sweep.
+`--impl reference-gpu --config c1|c2|c3` times the reference's own GPU kernels (built unchanged for
+sm_100a) on the same B200 and data; c4's 65,536 lists do not fit its probe selection.
 """
 import argparse
 import json
@@ -49,7 +51,8 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "reference-gpu"])
+    p.add_argument("--ref-tile", type=int, default=0, help="reference-gpu: tile size 64 or 256 (default by D)")
     p.add_argument("--config", default="c4")
     p.add_argument("--batch", type=int, default=0, help="queries per step (default: the config's B)")
     p.add_argument("--nprobe", type=int, default=0)
@@ -881,11 +884,124 @@ def run_reference(args, d: Dist):
     }
 
 
+def run_reference_gpu(args, d: Dist):
+    """The reference's own GPU search (src/trident_v4_kernels.cu, built unchanged for sm_100a into
+    oracle/_ref/gpu) on this B200, over the same rows, lists and queries as this library's arm.
+    `value` is its mode 2 (the lossless cascade); its mode 10 (exact cluster-major FP32) is reported
+    beside it. The same timing rules as this library's arm: W warm-up steps, K device-timed steps
+    with a 512 MB L2 flush between them. A sample of queries is checked against the oracle's exact
+    IVF-Flat over the reference's own probe sets (float32 coarse distances)."""
+    if d.rank != 0:
+        return None
+    import numpy as np
+    import torch
+
+    from oracle import oracle as O
+    from oracle import ref_gpu
+    from trident_b200 import SharedClusterStorage
+
+    try:
+        ref_gpu.load()
+    except Exception as e:
+        return {"impl": "reference-gpu", "unavailable": f"reference GPU module not built: {e}"}
+    cfg = workload_config(args)
+    if cfg.nlist > ref_gpu.MAX_NLIST:
+        return {"impl": "reference-gpu",
+                "unavailable": f"{cfg.name}: nlist {cfg.nlist} does not fit the reference's probe selection, which "
+                               f"holds a query's whole coarse row in shared memory (at most {ref_gpu.MAX_NLIST} lists "
+                               f"in 227 KB)"}
+    if cfg.K != ref_gpu.REF_K:
+        return {"impl": "reference-gpu", "unavailable": "the reference's GPU kernels hold K = 10 only"}
+    xb, xq, lids, c_np, l_np, mu_np, R_np, strong = make_clustering(args, d, cfg)
+    st = SharedClusterStorage(xb, lids, None, cfg.nlist, device=d.dev)
+    del xb, lids
+    torch.cuda.empty_cache()
+    B, nprobe = int(xq.shape[0]), cfg.nprobe
+    tile = args.ref_tile or (256 if cfg.D >= 256 else 64)
+    t0 = time.perf_counter()
+    ref = ref_gpu.RefGpuIndex(st.xb_sorted, st.orig_ids_sorted, st.cluster_vec_off.cpu().numpy(), c_np, mu_np,
+                              R_np, tile_size=tile, max_batch=B, max_nprobe=nprobe)
+    torch.cuda.synchronize()
+    log(f"[rank 0] reference arrays (tile {tile}) in {time.perf_counter() - t0:.1f}s")
+    xq_pin = torch.from_numpy(xq).pin_memory()
+    xq_dev = xq_pin.to(d.dev)
+
+    # oracle check of a sample under each mode, over the reference's own probe sets
+    n = min(B, args.check)
+    off = st.cluster_vec_off.cpu().numpy().astype(np.int64)
+    xs_h, perm_h = st.xb_sorted.cpu().numpy(), st.orig_ids_sorted.cpu().numpy()
+    checks = {}
+    for mode in (2, 10):
+        dd, ii, cids, _ = ref.search(xq_dev, nprobe, mode=mode)
+        torch.cuda.synchronize()
+        dd, ii, cids = dd.cpu().numpy()[:n], ii.cpu().numpy()[:n], cids.cpu().numpy()[:n]
+        od, oi = O.ivf_search(xq[:n], cids, off, xs_h, perm_h, cfg.K)
+        fin = np.isfinite(od)
+        checks[mode] = {"queries": n, "ids_identical": bool(np.array_equal(ii, oi)),
+                        "distances_bit_identical": bool(np.array_equal(dd[fin].view(np.uint32),
+                                                                       od[fin].view(np.uint32)))}
+    del xs_h, perm_h
+    log(f"[rank 0] reference vs oracle over its own probe sets: {checks}")
+
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=d.dev)
+    stream = torch.cuda.current_stream(d.dev)
+    timed = {}
+    clocks = ClockSampler(d.local)
+    clocks.start()
+    time.sleep(0.3)
+    for mode in (2, 10):
+        for _ in range(args.warmup):
+            ref.search(xq_dev, nprobe, mode=mode)
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for s in range(args.steps):
+            flush.fill_(s & 0xFF)
+            evs[s][0].record(stream)
+            ref.search(xq_dev, nprobe, mode=mode)
+            evs[s][1].record(stream)
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in evs) / args.steps
+        timed[mode] = {"qps": round(B / (ms * 1e-3), 1), "ms_per_step": round(ms, 4)}
+    # end to end, mode 2: H2D of the pinned queries, the search, D2H of the top-K, per step in order
+    out_d = torch.empty((B, cfg.K), dtype=torch.float32, pin_memory=True)
+    out_i = torch.empty((B, cfg.K), dtype=torch.int64, pin_memory=True)
+    xq_buf = torch.empty_like(xq_dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        xq_buf.copy_(xq_pin, non_blocking=True)
+        dd, ii, _, _ = ref.search(xq_buf, nprobe, mode=2)
+        out_d.copy_(dd, non_blocking=True)
+        out_i.copy_(ii, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    return {
+        "metric": METRIC, "value": timed[2]["qps"], "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": timed[2]["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32", "data": data_desc(cfg),
+        "impl": "reference-gpu",
+        "config": {"workload": f"{cfg.name}: N={cfg.N} D={cfg.D} nlist={cfg.nlist} nprobe={nprobe} K={cfg.K} B={B}",
+                   "global_batch": B, "tile_size": tile,
+                   "kernels": "the reference's src/trident_v4_kernels.cu, unchanged, -O3 --use_fast_math, sm_100a",
+                   "l2": "a 512 MB L2 flush between timed steps (outside the step events)",
+                   "modes": {"2 (cascade)": timed[2], "10 (cm_fp32)": timed[10]}},
+        "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": UNIT, "h2d_bytes_per_step": int(xq_pin.numel() * 4),
+                "d2h_bytes_per_step": int(out_d.numel() * 4 + out_i.numel() * 8),
+                "method": "mode 2; per step H2D of the pinned queries, the search, D2H of the top-K, in order on "
+                          "one stream; CUDA events around all steps"},
+        "clocks": clk,
+        "lossless_check": {"vs": "the oracle's exact IVF-Flat over the reference's own probe sets",
+                           "mode_2": checks[2], "mode_10": checks[10]},
+    }
+
+
 def main():
     args = parse_args()
     d = Dist()
-    if args.impl == "reference":
-        # the CPU reference runs on rank 0 alone; other ranks exit without work
+    if args.impl in ("reference", "reference-gpu"):
+        # the reference arms run on rank 0 alone; other ranks exit without work
         if d.rank != 0:
             return 0
         d.launched = d.world  # the job's GPU count, reported; rank 0 alone runs, without a process group
@@ -894,12 +1010,14 @@ def main():
     try:
         if args.impl == "reference":
             res = run_reference(args, d)
+        elif args.impl == "reference-gpu":
+            res = run_reference_gpu(args, d)
         elif args.sweep:
             res = run_sweep(args, d)
         else:
             res = run_ours(args, d)
     finally:
-        if args.impl != "reference":
+        if args.impl not in ("reference", "reference-gpu"):
             d.close()
     if d.rank == 0 and res is not None:
         print(json.dumps(res), flush=True)

@@ -13,6 +13,11 @@ the host CPU that will run it is not known at build time; ref_cpu.py loads the o
 supports.
 It runs only where the reference checkout is present (TRIDENT_REFERENCE_ROOT, else a `reference`
 directory beside the repository root); machines without it use the prebuilt files.
+
+build_gpu() also compiles the reference's GPU search, src/trident_v4_kernels.cu, unchanged, as the
+torch extension its own suite JIT-builds (benchmarks/phase4a_suite.py:65-72, same flags: -O3
+--use_fast_math -lineinfo) for sm_100a, into oracle/_ref/gpu/. ref_gpu.py drives it; tests use it to
+pin the reference's GPU summation order against the oracle on the B200.
 """
 import os
 import re
@@ -23,6 +28,9 @@ OUT = os.path.join(HERE, "_ref")
 REF_ROOT = os.environ.get("TRIDENT_REFERENCE_ROOT",
                           os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 REF_FILE = os.path.join(REF_ROOT, "benchmarks", "phase8_ooc_100m_4080.py")
+REF_GPU_FILE = os.path.join(REF_ROOT, "src", "trident_v4_kernels.cu")
+GPU_NAME = "trident_ref_v4"
+GPU_DIR = os.path.join(OUT, "gpu")
 LEVELS = {"x86-64-v3": "trident_ref_cpu_v3", "x86-64-v4": "trident_ref_cpu_v4"}
 
 _THREADS_HELPER = """
@@ -81,6 +89,30 @@ def build(force: bool = False, quiet: bool = True) -> bool:
     return True
 
 
+def gpu_module_path() -> str:
+    return os.path.join(GPU_DIR, f"{GPU_NAME}.so")
+
+
+def build_gpu(force: bool = False, quiet: bool = True) -> bool:
+    """Compile the reference GPU extension for sm_100a (nvcc cross-compiles; no GPU needed).
+    Returns False when the reference is not mounted."""
+    if not os.path.exists(REF_GPU_FILE):
+        return False
+    out = gpu_module_path()
+    if not force and os.path.exists(out) and os.path.getmtime(out) >= os.path.getmtime(REF_GPU_FILE):
+        return True
+    os.makedirs(GPU_DIR, exist_ok=True)
+    from torch.utils.cpp_extension import load
+
+    # an explicit -gencode makes torch add no arch flags of its own
+    load(name=GPU_NAME, sources=[REF_GPU_FILE], build_directory=GPU_DIR,
+         extra_cflags=["-O3"],
+         extra_cuda_cflags=["-O3", "--use_fast_math", "-lineinfo", "-gencode", "arch=compute_100a,code=sm_100a"],
+         verbose=not quiet)
+    return True
+
+
 if __name__ == "__main__":
     ok = build(force="--force" in sys.argv, quiet=False)
-    print("built" if ok else "reference not mounted; nothing built")
+    ok_gpu = build_gpu(force="--force" in sys.argv, quiet=False)
+    print("built" if ok and ok_gpu else "reference not mounted; nothing built")

@@ -67,3 +67,31 @@ def assert_same_topk(d, i, od, oi, exact_dist=True, rtol=1e-5):
             f"max |dd| = {np.abs(d[fin] - od[fin]).max()}"
     else:
         np.testing.assert_allclose(d[fin], od[fin], rtol=rtol)
+
+
+def build_config_index(cfg, centroid_mode, seed=7, tile_size=None):
+    """Rows and queries of cfg's distribution and an index over them (needs a GPU). Centroids from a
+    short k-means ("kmeans") or sampled rows ("rows": integer-valued for the integer mixtures, so
+    exact float64 ties occur at the nprobe boundary). Returns (xb, xq, centroids, list_ids, index)."""
+    import torch
+
+    from trident_b200 import SharedClusterStorage, TridentV4Index, choose_tile, datasets as ds
+    from trident_b200.clustering import assign, train_clustering
+
+    xb = ds.generate_np(cfg, cfg.N, ds.SEED_BASE)
+    xq = ds.generate_np(cfg, cfg.B, ds.SEED_QUERY)
+    if centroid_mode == "kmeans":
+        cent, lids, _, mu, R, _ = train_clustering(xb, cfg.nlist, sample_size=min(cfg.N, 16 * cfg.nlist), niter=4,
+                                                   device="cuda:0")
+    else:
+        rng = np.random.default_rng(seed)
+        cent = np.ascontiguousarray(xb[rng.choice(cfg.N, cfg.nlist, replace=False)])
+        xg = torch.from_numpy(xb).cuda()
+        lids = assign(xg, torch.from_numpy(cent).cuda()).to(torch.int32).cpu().numpy()
+        del xg
+        mu = np.zeros(cfg.D)
+        R = np.linalg.qr(rng.standard_normal((cfg.D, cfg.D)))[0]
+    st = SharedClusterStorage(xb, lids, None, cfg.nlist, device="cuda:0")
+    idx = TridentV4Index(st, cent, mu, R, tile_size=tile_size or choose_tile(cfg.D), device="cuda:0",
+                         max_batch=cfg.B, max_nprobe=cfg.nprobe)
+    return xb, xq, cent, lids, idx

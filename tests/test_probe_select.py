@@ -14,36 +14,13 @@ the search's top-K (ids identical, distances bit-identical) against the oracle's
 import numpy as np
 import pytest
 
-from helpers import assert_same_topk, oracle_search
+from helpers import assert_same_topk, build_config_index, oracle_search
 
 pytestmark = pytest.mark.gpu
 
 
 def _build(cfg, centroid_mode, seed=7):
-    """Rows and queries of cfg's distribution; centroids from a short k-means ("kmeans") or sampled
-    rows ("rows": integer-valued for the int mixtures, so exact float64 ties occur at the boundary)."""
-    import torch
-
-    from trident_b200 import SharedClusterStorage, TridentV4Index, choose_tile, datasets as ds
-    from trident_b200.clustering import assign, train_clustering
-
-    xb = ds.generate_np(cfg, cfg.N, ds.SEED_BASE)
-    xq = ds.generate_np(cfg, cfg.B, ds.SEED_QUERY)
-    if centroid_mode == "kmeans":
-        cent, lids, _, mu, R, _ = train_clustering(xb, cfg.nlist, sample_size=min(cfg.N, 16 * cfg.nlist), niter=4,
-                                                   device="cuda:0")
-    else:
-        rng = np.random.default_rng(seed)
-        cent = np.ascontiguousarray(xb[rng.choice(cfg.N, cfg.nlist, replace=False)])
-        xg = torch.from_numpy(xb).cuda()
-        lids = assign(xg, torch.from_numpy(cent).cuda()).to(torch.int32).cpu().numpy()
-        del xg
-        mu = np.zeros(cfg.D)
-        R = np.linalg.qr(rng.standard_normal((cfg.D, cfg.D)))[0]
-    st = SharedClusterStorage(xb, lids, None, cfg.nlist, device="cuda:0")
-    idx = TridentV4Index(st, cent, mu, R, tile_size=choose_tile(cfg.D), device="cuda:0", max_batch=cfg.B,
-                         max_nprobe=cfg.nprobe)
-    return xb, xq, cent, lids, idx
+    return build_config_index(cfg, centroid_mode, seed)
 
 
 def _coarse_matches_oracle(idx, xq, cent, nprobe):
