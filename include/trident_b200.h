@@ -28,7 +28,7 @@
 extern "C" {
 #endif
 
-#define TRIDENT_ABI_VERSION 1
+#define TRIDENT_ABI_VERSION 2
 
 enum trident_status {
     TRIDENT_OK = 0,
@@ -63,7 +63,7 @@ typedef struct trident_index {
     int32_t nlist;                   /* IVF lists                                        */
     int32_t tile_size;               /* rows per tile: 128 or 256                        */
     int32_t num_blocks;              /* D_pad / 32                                       */
-    int32_t reserved0;
+    int32_t flags;                   /* TRIDENT_INDEX_* bits, 0 by default                */
     const float*   xb_sorted;        /* [N, D] rows in list order                        */
     const int32_t* orig_ids_sorted;  /* [N] original id of each sorted row               */
     const int64_t* list_row_off;     /* [nlist+1] (reference: cluster_vec_off, int32)    */
@@ -78,7 +78,18 @@ typedef struct trident_index {
     const double*  pca_rot;          /* [D, D] row-major; column d is component d        */
     float centroid_norm_max;         /* max_c ||c||, for the coarse GEMM error bound     */
     float lb_rel_slack;              /* relative slack rho of the Stage-Y prune test     */
+    /* Optional [total_tiles * tile_size], in code-slot order (tile t, row v of the tile): the row's
+     * sum_d (code_d delta_d)^2 in float64, rounded down to float (0 for empty slots). With it the
+     * cascade runs Stage Y on the tensor cores (an 8-bit MMA per 32-dim code block and a bound over
+     * all dims at once) when D_pad <= 256 and B * nprobe >= 32768, where it is the faster of the two
+     * (or always, with TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS); NULL keeps the CUDA-core Stage Y.
+     * Results are the same either way. */
+    const float*   row_p;
 } trident_index;
+
+/* trident_index.flags: run Stage Y on the tensor cores for every cascade search (given row_p),
+ * not only where the library's size rule picks it (D_pad <= 256 and B * nprobe >= 32768). */
+#define TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS 1
 
 /* Statistics slots of the optional int64 `stats` array (at least TRIDENT_STATS_LEN entries, zeroed
  * by the caller). Slots 0-3 are the reference's stats_buf counters (:700-704, :774-795, :921-923). */

@@ -44,7 +44,7 @@ def test_every_declared_symbol_is_exported(L):
 
 
 def test_version(L):
-    assert L.trident_version() == 1
+    assert L.trident_version() == 2
 
 
 def test_noalloc_size_matches_the_header(L):

@@ -1,0 +1,132 @@
+"""Stage Y on the tensor cores (tb_filter.cu) against the oracle and the CUDA-core Stage Y (needs a
+B200 for the searches; the row_p check runs anywhere).
+
+The tensor-core filter bounds each (query, row) pair from an exact int8 MMA of the row's SQ8 codes
+with the query's split weights, and refines the survivors in the reference's FP32 order, so its
+results must be bit-identical to the oracle's exact IVF-Flat and to the CUDA-core path's. The
+library picks it by size (TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS forces it, which the small cases here
+need); the status-word checks repeat the wait-limit tests on this kernel.
+"""
+import numpy as np
+import pytest
+
+from helpers import CASE_NAMES, assert_same_topk, build_config_index, build_index, load_case, oracle_search
+
+
+def _search(idx, xq, nprobe, K, mode=2):
+    import torch
+
+    d, i, _ = idx.search(torch.from_numpy(xq).cuda(), nprobe, mode=mode, k=K)
+    torch.cuda.synchronize()
+    return d.cpu().numpy().copy(), i.cpu().numpy().copy()
+
+
+def _stats(idx, xq, nprobe, K):
+    import torch
+
+    st = torch.zeros(8, dtype=torch.int64, device="cuda")
+    idx.search(torch.from_numpy(xq).cuda(), nprobe, mode=2, k=K, stats_buf=st)
+    torch.cuda.synchronize()
+    return st.cpu().numpy()
+
+
+def test_row_p_is_the_rounded_down_row_term():
+    """row_p[slot] = sum_d (code_d delta_d)^2 of the slot's row, in float64 rounded down to float32."""
+    from helpers import sorted_storage  # noqa: F401
+
+    f = load_case("g2_decay_c2")
+    idx = build_index(f, device="cpu")
+    h = idx.host_arrays()
+    T, D_pad, nb = idx.tile_size, idx.D_pad, idx.num_blocks
+    codes = h["codes"].reshape(-1, nb, T, 32).transpose(0, 2, 1, 3).reshape(-1, T, D_pad).astype(np.float64)
+    toff = h["tile_off"]
+    lists = np.repeat(np.arange(idx.nlist), np.diff(toff))
+    p64 = ((codes * h["delta"][lists][:, None, :].astype(np.float64)) ** 2).sum(-1).reshape(-1)
+    rp = idx.row_p().numpy().astype(np.float64)
+    assert rp.shape == p64.shape
+    assert (rp <= p64).all()
+    assert np.allclose(rp, p64, rtol=1e-6, atol=0)
+
+
+def test_set_stage_y_rejects_unknown_modes():
+    f = load_case("g1_int_c1")
+    idx = build_index(f, device="cpu")
+    with pytest.raises(ValueError):
+        idx.set_stage_y("sometimes")
+    idx.set_stage_y("off")
+    assert idx.stage_y == "off"
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", CASE_NAMES)
+@pytest.mark.parametrize("K", [10, 100])
+def test_forced_tensor_stage_y_equals_oracle_on_fixtures(name, K):
+    f = load_case(name)
+    idx = build_index(f, max_k=100)
+    idx.set_stage_y("always")
+    nprobe = int(f["nprobe"])
+    od, oi, _ = oracle_search(f["xb"], f["list_ids"], f["centroids"], f["xq"], nprobe, K)
+    d, i = _search(idx, f["xq"], nprobe, K)
+    assert idx.status() == 0
+    assert_same_topk(d, i, od, oi)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("cfg_name,over", [
+    # c4 shape: integer rows, D = 128, 1,526 rows per list, nprobe 256 (about 39 queries per list)
+    ("c4", dict(N=1_000_000, nlist=656, nprobe=256, B=1000, K=10, n_comp=41)),
+    # c3 shape: unit-norm real rows, D = 96 (D_pad 96: three code blocks)
+    ("c3", dict(N=500_000, nlist=1024, nprobe=32, B=2000, K=10)),
+])
+def test_tensor_and_cuda_core_stage_y_agree_at_config_shapes(cfg_name, over):
+    from trident_b200 import datasets as ds
+
+    ncomp = over.pop("n_comp", None)
+    cfg = ds.scaled(ds.CONFIGS[cfg_name], **over)
+    if ncomp:
+        cfg = ds.Config(**{**cfg.__dict__, "n_comp": ncomp})
+    xb, xq, cent, lids, idx = build_config_index(cfg, "kmeans")
+    od, oi, _ = oracle_search(xb, lids, cent, xq[:64], cfg.nprobe, cfg.K)
+    results = {}
+    for mode in ("off", "always", "auto"):
+        idx.set_stage_y(mode)
+        results[mode] = _search(idx, xq, cfg.nprobe, cfg.K)
+        assert idx.status() == 0
+        assert_same_topk(results[mode][0][:64], results[mode][1][:64], od, oi)
+    for mode in ("always", "auto"):
+        assert np.array_equal(results[mode][1], results["off"][1])
+        assert np.array_equal(results[mode][0].view(np.uint32), results["off"][0].view(np.uint32))
+    # the same candidates enter Stage Y on both paths; the tensor-core filter scans all dims of each
+    idx.set_stage_y("off")
+    s_off = _stats(idx, xq, cfg.nprobe, cfg.K)
+    idx.set_stage_y("always")
+    s_on = _stats(idx, xq, cfg.nprobe, cfg.K)
+    assert s_on[0] == s_off[0]
+    assert s_on[1] == s_on[0] * idx.D_pad
+    assert 0 < s_on[2] < 0.01 * s_on[0]  # survivors: a small share of the candidates
+
+
+@pytest.mark.gpu
+def test_tensor_stage_y_waits_that_give_up_mark_every_result():
+    import torch
+
+    from trident_b200 import _lib
+
+    f = load_case("g3_norm_c3")
+    idx = build_index(f)
+    idx.set_stage_y("always")
+    nprobe, K = int(f["nprobe"]), int(f["K"])
+    try:
+        for limits, status in (((0, -1), _lib.STATUS_LOCK_TIMEOUT), ((-1, 0), _lib.STATUS_MMA_TIMEOUT)):
+            _lib.set_wait_limits(*limits)
+            d, i = _search(idx, f["xq"], nprobe, K)
+            assert np.isnan(d).all() and (i == -2).all()
+            assert idx.status() & status
+            _lib.set_wait_limits(-1, -1)
+            d, i = _search(idx, f["xq"], nprobe, K)
+            assert idx.status() == 0
+            od, oi, _ = oracle_search(f["xb"], f["list_ids"], f["centroids"], f["xq"], nprobe, K)
+            assert_same_topk(d, i, od, oi)
+    finally:
+        _lib.set_wait_limits(-1, -1)
+    torch.cuda.synchronize()

@@ -33,6 +33,7 @@ QINFO_LEN = 4
 PHASES = ("coarse", "pairs", "seed", "scan", "merge")
 
 # device-side status word of a workspace (trident_workspace_status)
+INDEX_TENSOR_STAGE_Y_ALWAYS = 1
 STATUS_OK = 0
 STATUS_LOCK_TIMEOUT = 1
 STATUS_MMA_TIMEOUT = 2
@@ -58,7 +59,7 @@ class TridentIndexDesc(ctypes.Structure):
         ("nlist", ctypes.c_int32),
         ("tile_size", ctypes.c_int32),
         ("num_blocks", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
         ("xb_sorted", ctypes.c_void_p),
         ("orig_ids_sorted", ctypes.c_void_p),
         ("list_row_off", ctypes.c_void_p),
@@ -73,6 +74,7 @@ class TridentIndexDesc(ctypes.Structure):
         ("pca_rot", ctypes.c_void_p),
         ("centroid_norm_max", ctypes.c_float),
         ("lb_rel_slack", ctypes.c_float),
+        ("row_p", ctypes.c_void_p),
     ]
 
 

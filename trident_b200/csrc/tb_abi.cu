@@ -292,7 +292,7 @@ static int stage_seed(const trident_index* idx, const float* xq, int32_t B, int3
     int rc_join = 0;
     SideStream* ss = nullptr;
     TB_TRY(side_stream(&ss), "side stream");
-    const int G = scan_group_size(*idx, K);
+    const int G = filter_eligible(*idx, K, lb, ub_seed == 2, (int64_t)B * nprobe) ? filter_group_size(*idx, K) : scan_group_size(*idx, K);
     TB_TRY(mark(TRIDENT_PHASE_PAIRS), "event");
     TB_TRY(cudaEventRecord(ss->fork2, st), "fork");
     TB_TRY(cudaStreamWaitEvent(ss->s, ss->fork2, 0), "fork");
@@ -319,14 +319,19 @@ static int stage_scan(const trident_index* idx, const float* xq, int32_t B, int3
     ScanLaunch sl;
     sl.K = K;
     sl.nprobe = nprobe;
-    sl.G = scan_group_size(*idx, K);
+    sl.filter = filter_eligible(*idx, K, lb, ub_seed == 2, (int64_t)B * nprobe) ? 1 : 0;
+    sl.G = sl.filter ? filter_group_size(*idx, K) : scan_group_size(*idx, K);
     sl.lb = lb ? 1 : 0;
     sl.pass = 1;
     sl.ub_seed = (lb && ub_seed == 2) ? 1 : 0;
     sl.max_items = B * nprobe;
     sl.item_base = 0;
     TB_TRY(mark(TRIDENT_PHASE_SCAN), "event");
-    TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan");
+    if (sl.filter) {
+        TB_TRY(launch_filter(*idx, xq, ws, sl, sp, st), "tensor-core stage Y");
+    } else {
+        TB_TRY(launch_scan(*idx, xq, ws, sl, sp, st), "scan");
+    }
     TB_TRY(mark(TRIDENT_PHASE_MERGE), "event");
     TB_TRY(launch_merge(ws, B, K, nprobe, 0, nprobe, nullptr, out_d, out_i, st), "merge");
     g_launches += 2;

@@ -38,6 +38,7 @@
 
 #include "tb_common.cuh"
 #include "tb_internal.h"
+#include "tb_tc.cuh"
 
 namespace tb {
 
@@ -57,7 +58,6 @@ struct EpiShape {
 };
 constexpr int kGOpBytes = kGM * kGK * 4; // one operand split of one stage: 16 KB
 constexpr uint32_t kGTmemCols = 2 * kGN; // two accumulators of 128 columns
-constexpr uint32_t kGDrainPolls = 1u << 22;
 
 static_assert(kGM == kGN, "square tiles: A and B stage buffers have the same size");
 static_assert(EpiShape<false>::kCols == kCoarseMinSpan, "one row minimum per epilogue warp and tile");
@@ -73,7 +73,7 @@ struct GemmShape {
 constexpr uint32_t kGIdesc =
     (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kGN >> 3) << 17) | ((uint32_t)(kGM >> 4) << 24);
 
-__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+using tc::saddr;
 
 // K-major descriptor of a 128-byte-swizzled tile (the layout a SWIZZLE_128B tensor copy of 32
 // floats x 128 rows writes: row r at r * 128 bytes, its 16-byte chunk j at chunk j ^ (r % 8)):
@@ -93,60 +93,19 @@ __device__ __forceinline__ void gmma(uint32_t d_tmem, uint64_t a, uint64_t b, ui
         "l"(a), "l"(b), "r"(kGIdesc), "r"(accumulate));
 }
 
-__device__ __forceinline__ void gcommit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(saddr(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ void gbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void gbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
-}
-
-__device__ __forceinline__ void gbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
-}
-
-// One poll; a thread that finds the phase incomplete may be suspended, for at most about 256 ns (the
-// suspend-time hint), so kGDrainPolls polls take about a second at most.
-__device__ __forceinline__ bool gbar_try(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, 256;\n\t"
-        "selp.b32 %0, 1, 0, P1;\n\t}\n"
-        : "=r"(ok)
-        : "r"(saddr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-// Bounded wait for the phase of `parity`; gives up after `polls` polls or once another warp has set
-// *abort. Returns whether the phase completed.
+__device__ __forceinline__ void gcommit(uint64_t* bar) { tc::mma_commit(bar); }
+__device__ __forceinline__ void gbar_init(uint64_t* bar, uint32_t count) { tc::bar_init(bar, count); }
+__device__ __forceinline__ void gbar_arrive(uint64_t* bar) { tc::bar_arrive(bar); }
+__device__ __forceinline__ void gbar_expect_tx(uint64_t* bar, uint32_t bytes) { tc::bar_expect_tx(bar, bytes); }
 __device__ __forceinline__ bool gwait(uint64_t* bar, uint32_t parity, uint32_t polls, volatile int* abort) {
-    for (uint32_t i = 0; i < polls; ++i) {
-        if (gbar_try(bar, parity)) return true;
-        if (*abort) return false;
-    }
-    return false;
+    return tc::bar_wait(bar, parity, polls, abort);
 }
-
-// Bounded wait without an abort check (draining after an abort).
-__device__ __forceinline__ void gdrain(uint64_t* bar, uint32_t parity) {
-    for (uint32_t i = 0; i < kGDrainPolls; ++i)
-        if (gbar_try(bar, parity)) return;
-}
+__device__ __forceinline__ void gdrain(uint64_t* bar, uint32_t parity) { tc::bar_drain(bar, parity); }
 
 // One K = 32 slice (128 bytes per row) of 128 rows starting at `row0` into `dst` (16 KB, 1024-byte
 // aligned), 128-byte swizzled.
 __device__ __forceinline__ void tma_slice(void* dst, const CUtensorMap* map, int row0, int kc, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            saddr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(kc * kGK), "r"(row0), "r"(saddr(bar))
-        : "memory");
+    tc::tma_load_2d(dst, map, kc * kGK, row0, bar);
 }
 
 struct GemmParams {
@@ -497,6 +456,22 @@ cudaError_t launch_gemm(const CUtensorMap* maps, GemmParams p, cudaStream_t st) 
 }
 
 }  // namespace
+
+// 2-D view {32 bytes, rows} of the blocked SQ8 codes, one 32-dim block of one row per view row,
+// box {32, 128}, 32-byte swizzle: one copy writes one code block of 128 rows in the canonical K-major
+// SWIZZLE_32B layout of an 8-bit UMMA operand (row r at r * 32 bytes, its 16-byte half h at
+// h ^ ((r / 4) % 2)).
+bool make_codes_map(CUtensorMap* m, const uint8_t* codes, int64_t rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return false;
+    const cuuint64_t dims[2] = {32, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {32};
+    const cuuint32_t box[2] = {32, 128};
+    const cuuint32_t es[2] = {1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(codes), dims, strides, box, es,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_32B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 size_t coarse_split_bytes(const trident_index& idx, int B) {
     return ((size_t)B + (size_t)idx.nlist) * (size_t)idx.D_pad * 2 * sizeof(float);

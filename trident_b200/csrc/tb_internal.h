@@ -110,10 +110,17 @@ struct ScanLaunch {
     int ub_seed;     // 1: seed each item's threshold from SQ8 upper bounds first
     int max_items;   // upper bound on the item count of this pass
     int64_t item_base;  // index of this pass's first item in the item array
+    int filter;      // 1: Stage Y on the tensor cores (tb_filter.cu) instead of scan_kernel
 };
 cudaError_t launch_scan(const trident_index& idx, const float* xq, const Workspace& ws, const ScanLaunch& sl,
                         unsigned long long* stats, cudaStream_t st);
 int scan_group_size(const trident_index& idx, int K);
+// Stage Y on the tensor cores (tb_filter.cu): whether it serves this search, its queries per item,
+// and its launch (same items, thresholds and candidate slots as launch_scan).
+bool filter_eligible(const trident_index& idx, int K, bool lb, bool ub_items, int64_t pairs);
+int filter_group_size(const trident_index& idx, int K);
+cudaError_t launch_filter(const trident_index& idx, const float* xq, const Workspace& ws, const ScanLaunch& sl,
+                          unsigned long long* stats, cudaStream_t st);
 cudaError_t launch_merge(const Workspace& ws, int B, int K, int nprobe, int p_lo, int p_hi, uint32_t* tau_out,
                          float* out_d, int64_t* out_i, cudaStream_t st);
 cudaError_t launch_merge_shards(const float* d_in, const int64_t* i_in, int R, int B, int K, float* out_d,

@@ -266,12 +266,51 @@ class TridentV4Index:
         return self
 
     # ------------------------------------------------------------------------------------------
+    # Stage Y on the tensor cores (the library's tcgen05 8-bit filter) needs each code slot's
+    # sum_d (code_d delta_d)^2 (row_p). "auto" lets the library pick it where it is the faster
+    # (D_pad <= 256, B * nprobe >= 32768), "always" for every cascade search, "off" never. The
+    # results are identical in every setting.
+    stage_y = "auto"
+
+    def set_stage_y(self, mode: str) -> None:
+        if mode not in ("auto", "always", "off"):
+            raise ValueError(f"stage_y mode {mode!r}: expected 'auto', 'always' or 'off'")
+        self.stage_y = mode
+        self._desc = None
+
+    def row_p(self):
+        """[total_tiles * tile_size] float32 in code-slot order: sum_d (code_d delta_d)^2 of the slot's
+        row in float64, rounded down (0 for empty slots). Computed once from the codes and deltas."""
+        if getattr(self, "_row_p", None) is not None:
+            return self._row_p
+        torch = _torch()
+        T, nb, D_pad = self.tile_size, self.num_blocks, self.D_pad
+        tiles = max(self.total_tiles, 1)
+        out = torch.zeros(tiles * T, dtype=torch.float32, device=self.codes.device)
+        if self.total_tiles > 0:
+            toff = self.cluster_tile_off.to(out.device).long()
+            tile_list = torch.repeat_interleave(torch.arange(self.nlist, device=out.device), toff[1:] - toff[:-1])
+            codes = self.codes.view(tiles, nb, T, 32)
+            dl = self.delta_pad.to(out.device).double()
+            step = max(1, (1 << 25) // (T * D_pad))  # about 256 MB of float64 per chunk
+            for s in range(0, self.total_tiles, step):
+                e = min(self.total_tiles, s + step)
+                x = codes[s:e].permute(0, 2, 1, 3).reshape(e - s, T, D_pad).double() * dl[tile_list[s:e]].unsqueeze(1)
+                p64 = (x * x).sum(-1) * (1.0 - 1e-12)
+                p32 = p64.float()
+                p32 = torch.where(p32.double() > p64, torch.nextafter(p32, torch.zeros_like(p32)), p32)
+                out[s * T:e * T] = p32.reshape(-1)
+                del x, p64, p32
+        self._row_p = out
+        return out
+
     def desc(self) -> _lib.TridentIndexDesc:
         if self._desc is None:
             s = self.storage
             d = _lib.TridentIndexDesc()
             d.N, d.D, d.D_pad, d.nlist = self.N, self.D, self.D_pad, self.nlist
-            d.tile_size, d.num_blocks, d.reserved0 = self.tile_size, self.num_blocks, 0
+            d.tile_size, d.num_blocks = self.tile_size, self.num_blocks
+            d.flags = _lib.INDEX_TENSOR_STAGE_Y_ALWAYS if self.stage_y == "always" else 0
             d.xb_sorted = _ptr(s.xb_sorted)
             d.orig_ids_sorted = _ptr(s.orig_ids_sorted)
             d.list_row_off = _ptr(s.cluster_vec_off)
@@ -282,6 +321,7 @@ class TridentV4Index:
             d.pca_mean, d.pca_rot = _ptr(self.pca_mean), _ptr(self.pca_rot)
             d.centroid_norm_max = self.centroid_norm_max
             d.lb_rel_slack = self.lb_rel_slack
+            d.row_p = _ptr(self.row_p()) if self.stage_y != "off" else None
             _lib.check(_lib.lib().trident_index_check(d))
             self._desc = d
         return self._desc
