@@ -30,9 +30,9 @@
 //               128 rows x 32 bytes of codes, 32-byte swizzled (the blocked code layout holds a
 //               block of a tile's rows contiguously, so no repacking is needed);
 //   warp 1      MMA issuer: per sub-tile nb MMAs (K = 32 each) into one of two accumulators;
-//   warps 2-17  epilogue: build the next item's B operand (the s8 weights, written in the same
+//   warps 2-13  epilogue: build the next item's B operand (the s8 weights, written in the same
 //               swizzled layout) while the MMAs of the current item run, then read each sub-tile's
-//               accumulator (4 warps per tensor-memory lane quarter, split over the queries), test
+//               accumulator (3 warps per tensor-memory lane quarter, split over the queries), test
 //               the bound and refine the survivors.
 // Every wait is bounded. A wait that gives up sets the status word (TRIDENT_STATUS_MMA_TIMEOUT;
 // the merge then marks every result), the producer drains its copies, the MMA warp its last
@@ -56,10 +56,12 @@ namespace {
 constexpr int kFM = 128;                       // rows per sub-tile (UMMA M)
 constexpr int kFStages = 8;                    // code-block stages
 constexpr int kFStageBytes = kFM * 32;         // one 32-dim block of 128 rows
-constexpr int kFEpiWarps = 16;                 // four per tensor-memory lane quarter
+constexpr int kFEpiWarps = 12;                 // three per tensor-memory lane quarter
+constexpr int kFParts = kFEpiWarps / 4;        // epilogue warps sharing a lane quarter (split the queries)
 constexpr int kFThreads = 64 + 32 * kFEpiWarps;
 constexpr int kFMaxG = 64;                     // queries per item
 constexpr int kFMaxN = 2 * kFMaxG;             // accumulator columns per sub-tile
+constexpr int kFQW = ((kFMaxG + kFParts - 1) / kFParts + 7) / 8 * 8;  // queries per epilogue warp, at most
 constexpr uint32_t kFTmemCols = 2 * kFMaxN;    // two accumulators
 constexpr int kFSmemLimit = 227 * 1024;
 constexpr int kFStatic = 8 * 1024;             // static shared memory and reserve
@@ -157,6 +159,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
     __shared__ int32_t s_qid[kFMaxG], s_pp[kFMaxG], s_lock[kFMaxG];
     __shared__ float s_tau[kFMaxG], s_sig[kFMaxG];
     __shared__ volatile float s_phi[kFMaxG];
+    __shared__ unsigned s_msk[kFEpiWarps][kFQW];  // per epilogue warp: survivor ballots of its queries
 
     unsigned char* smem = reinterpret_cast<unsigned char*>(
         (reinterpret_cast<uintptr_t>(f_smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -300,7 +303,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
         const int ew = warp - 2;                 // 0 .. kFEpiWarps-1
         const int etid = tid - 64;               // 0 .. 32 kFEpiWarps - 1
         const int quarter = warp & 3;            // tensor-memory lanes this warp may read
-        const int part = ew >> 2;                // which quarter of the item's column chunks
+        const int part = ew >> 2;                // which share of the item's queries
         unsigned long long st_cand = 0, st_surv = 0, st_ins = 0, st_items = 0;
         bool live = true;                        // false once a wait gave up: no more work, same barriers
         auto stop = [&]() {
@@ -445,7 +448,10 @@ __global__ void __launch_bounds__(kFThreads, 1)
             if (etid == 0) ++st_items;
             epi_sync();
 
-            const int nchunk = round16(2 * n) / 8;  // 8-column chunks: four queries each
+            // this warp's queries: a contiguous share of the item's, two accumulator columns each
+            const int qper = (n + kFParts - 1) / kFParts;
+            const int jb = part * qper;
+            const int jn = max(0, min(n, jb + qper) - jb);
             for (int s = 0; s < ns; ++s, ++g) {
                 const int acc = g & 1;
                 const int rl = s * kFM + quarter * 32 + lane;  // list-local row of this lane
@@ -458,76 +464,93 @@ __global__ void __launch_bounds__(kFThreads, 1)
                 if (!__all_sync(TB_FULL, w)) stop();
                 if (!live) continue;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-                const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kFMaxN);
-                for (int ch = part; ch < nchunk; ch += 4) {
-                    uint32_t r[8];
-                    asm volatile(
-                        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
-                        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
-                          "=r"(r[7])
-                        : "r"(taddr + (uint32_t)(ch * 8)));
-                    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                const uint32_t taddr =
+                    tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(acc * kFMaxN) + (uint32_t)(2 * jb);
+                // per group of eight queries: the loads (jn is warp-uniform), one wait, the bound; the
+                // ballots with survivors go to shared memory, their query slots to the bits of `nz`
+                uint32_t nz = 0;
 #pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) {
-                        const int j = ch * 4 + qq;
-                        if (j >= n) break;
-                        const float2 qc = s_qc[ib][j];
-                        const int32_t hi = (int32_t)r[2 * qq], lo = (int32_t)r[2 * qq + 1];
-                        const float v = fmaf(qc.x, (float)(hi * 254 + lo), P + qc.y);
-                        const bool alive = valid && v <= s_phi[j];
-                        st_cand += valid ? 1ull : 0ull;
-                        unsigned m = __ballot_sync(TB_FULL, alive);
-                        while (m) {  // refine each survivor (whole warp) and insert it under the lock
-                            const int sl = __ffs(m) - 1;
-                            m &= m - 1;
-                            if (lane == 0) ++st_surv;
-                            const int64_t grow = r0 + (int64_t)(s * kFM + quarter * 32 + sl);
-                            const int q = s_qid[j];
-                            const float dist =
-                                exact_dist_warp<VEC4, 4>(a.xb + grow * D, a.xq + (int64_t)q * D, D, lane);
-                            const int32_t id = __ldg(a.oid + grow);
-                            int got = 0;
-                            if (lane == 0) {
-                                for (uint32_t spin = 0; spin < a.lock_spins; ++spin) {
-                                    if (atomicCAS(&s_lock[j], 0, 1) == 0) {
-                                        got = 1;
-                                        break;
-                                    }
-                                    __nanosleep(64);
+                for (int g8 = 0; g8 < kFQW; g8 += 8) {
+                    if (g8 < jn) {
+                        uint32_t r[16];
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            if (g8 + i < jn)
+                                asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];"
+                                             : "=r"(r[2 * i]), "=r"(r[2 * i + 1])
+                                             : "r"(taddr + (uint32_t)(2 * (g8 + i))));
+                        }
+                        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            if (g8 + i < jn) {
+                                const float2 qc = s_qc[ib][jb + g8 + i];
+                                const float v =
+                                    fmaf(qc.x, (float)((int32_t)r[2 * i] * 254 + (int32_t)r[2 * i + 1]), P + qc.y);
+                                const unsigned mk = __ballot_sync(TB_FULL, valid && v <= s_phi[jb + g8 + i]);
+                                if (mk) {
+                                    nz |= 1u << (g8 + i);
+                                    if (lane == 0) s_msk[ew][g8 + i] = mk;
                                 }
                             }
-                            got = __shfl_sync(TB_FULL, got, 0);
-                            if (!got) {
-                                if (lane == 0) atomicOr(a.err, TRIDENT_STATUS_LOCK_TIMEOUT);
-                                continue;
-                            }
-                            __threadfence_block();
-                            float* ld = s_topd + j * KM;
-                            int32_t* li = s_topi + j * KM;
-                            const float d0 = __shfl_sync(TB_FULL, dist, 0);
-                            const int ins = list_offer<KM>(ld, li, K, lane == 0, d0, id, lane);
-                            if (lane == 0) {
-                                st_ins += (unsigned)ins;
-                                const float kth = ld[K - 1];
-                                const float gq = ld_volatile_f32(a.tau + q);
-                                const float t_old = s_tau[j];
-                                const float tq = fminf(fminf(t_old, kth), gq);
-                                if (tq < t_old) {
-                                    s_tau[j] = tq;
-                                    s_phi[j] = phi_of(prune_threshold(tq, s_sig[j], a.rho), E, s_slack[ib][j]);
-                                }
-                                __threadfence_block();
-                                atomicExch(&s_lock[j], 0);
-                                if (kth < t_old && kth < gq) atomicMin(a.tau + q, __float_as_uint(kth));
-                            }
-                            __syncwarp();
                         }
                     }
                 }
-                // the accumulator may be overwritten once every epilogue warp has read it
+                // the accumulator is in registers: release it before the survivors are refined
                 asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) tc::bar_arrive(&tempty[acc]);
+                st_cand += valid ? (unsigned long long)jn : 0ull;
+                while (nz) {
+                    const int i = __ffs(nz) - 1;
+                    nz &= nz - 1;
+                    const int j = jb + i;
+                    unsigned m = s_msk[ew][i];
+                    while (m) {  // refine each survivor (whole warp) and insert it under the lock
+                        const int sl = __ffs(m) - 1;
+                        m &= m - 1;
+                        if (lane == 0) ++st_surv;
+                        const int64_t grow = r0 + (int64_t)(s * kFM + quarter * 32 + sl);
+                        const int q = s_qid[j];
+                        const float dist = exact_dist_warp<VEC4, 2>(a.xb + grow * D, a.xq + (int64_t)q * D, D, lane);
+                        const int32_t id = __ldg(a.oid + grow);
+                        int got = 0;
+                        if (lane == 0) {
+                            for (uint32_t spin = 0; spin < a.lock_spins; ++spin) {
+                                if (atomicCAS(&s_lock[j], 0, 1) == 0) {
+                                    got = 1;
+                                    break;
+                                }
+                                __nanosleep(64);
+                            }
+                        }
+                        got = __shfl_sync(TB_FULL, got, 0);
+                        if (!got) {
+                            if (lane == 0) atomicOr(a.err, TRIDENT_STATUS_LOCK_TIMEOUT);
+                            continue;
+                        }
+                        __threadfence_block();
+                        float* ld = s_topd + j * KM;
+                        int32_t* li = s_topi + j * KM;
+                        const float d0 = __shfl_sync(TB_FULL, dist, 0);
+                        const int ins = list_offer<KM>(ld, li, K, lane == 0, d0, id, lane);
+                        if (lane == 0) {
+                            st_ins += (unsigned)ins;
+                            const float kth = ld[K - 1];
+                            const float gq = ld_volatile_f32(a.tau + q);
+                            const float t_old = s_tau[j];
+                            const float tq = fminf(fminf(t_old, kth), gq);
+                            if (tq < t_old) {
+                                s_tau[j] = tq;
+                                s_phi[j] = phi_of(prune_threshold(tq, s_sig[j], a.rho), E, s_slack[ib][j]);
+                            }
+                            __threadfence_block();
+                            atomicExch(&s_lock[j], 0);
+                            if (kth < t_old && kth < gq) atomicMin(a.tau + q, __float_as_uint(kth));
+                        }
+                        __syncwarp();
+                    }
+                }
             }
             epi_sync();
             // this item's per-query lists into the (query, probe) candidate slots
