@@ -29,7 +29,7 @@
 //   warp 0      TMA producer: per 128-row sub-tile of the list and per 32-dim block, one 2-D copy of
 //               128 rows x 32 bytes of codes, 32-byte swizzled (the blocked code layout holds a
 //               block of a tile's rows contiguously, so no repacking is needed);
-//   warp 1      MMA issuer: per sub-tile nb MMAs (K = 32 each) into one of two accumulators;
+//   warp 1      MMA issuer: per sub-tile nb MMAs (K = 32 each) into one of four accumulators;
 //   warps 2-13  epilogue: build the next item's B operand (the s8 weights, written in the same
 //               swizzled layout) while the MMAs of the current item run, then read each sub-tile's
 //               accumulator (3 warps per tensor-memory lane quarter, split over the queries), test
@@ -62,7 +62,8 @@ constexpr int kFThreads = 64 + 32 * kFEpiWarps;
 constexpr int kFMaxG = 64;                     // queries per item
 constexpr int kFMaxN = 2 * kFMaxG;             // accumulator columns per sub-tile
 constexpr int kFQW = ((kFMaxG + kFParts - 1) / kFParts + 7) / 8 * 8;  // queries per epilogue warp, at most
-constexpr uint32_t kFTmemCols = 2 * kFMaxN;    // two accumulators
+constexpr int kFAcc = 4;                       // accumulators in tensor memory (the MMAs run up to 3 ahead)
+constexpr uint32_t kFTmemCols = kFAcc * kFMaxN; // all 512 columns: one CTA per SM
 constexpr int kFSmemLimit = 227 * 1024;
 constexpr int kFStatic = 8 * 1024;             // static shared memory and reserve
 constexpr double kU = 5.9604644775390625e-08;  // float32 unit roundoff 2^-24
@@ -148,7 +149,7 @@ template <int KM, bool VEC4>
 __global__ void __launch_bounds__(kFThreads, 1)
     filter_kernel(const __grid_constant__ CUtensorMap mcodes, const FilterArgs a) {
     extern __shared__ unsigned char f_smem_raw[];
-    __shared__ __align__(8) uint64_t full[kFStages], empty[kFStages], tfull[2], tempty[2], bfull[2], bempty[2];
+    __shared__ __align__(8) uint64_t full[kFStages], empty[kFStages], tfull[kFAcc], tempty[kFAcc], bfull[2], bempty[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     // per B buffer (the item it was built for): per-query weight constants
@@ -184,9 +185,11 @@ __global__ void __launch_bounds__(kFThreads, 1)
             tc::bar_init(&full[s], 1);
             tc::bar_init(&empty[s], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kFAcc; ++b) {
             tc::bar_init(&tfull[b], 1);
             tc::bar_init(&tempty[b], kFEpiWarps);
+        }
+        for (int b = 0; b < 2; ++b) {
             tc::bar_init(&bfull[b], 1);
             tc::bar_init(&bempty[b], 1);
         }
@@ -261,8 +264,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
                 const uint32_t idesc = idesc_i8(N);
                 const uint32_t b0 = tc::saddr(s_b + (size_t)ib * nb * a.b_stride);
                 for (int s = 0; ok && s < ns; ++s, ++g) {
-                    const int acc = g & 1;
-                    if (!tc::bar_wait(&tempty[acc], ((g >> 1) & 1u) ^ 1u, a.polls, abort_flag)) {
+                    const int acc = g & (kFAcc - 1);
+                    if (!tc::bar_wait(&tempty[acc], ((g / kFAcc) & 1u) ^ 1u, a.polls, abort_flag)) {
                         ok = false;
                         break;
                     }
@@ -288,7 +291,7 @@ __global__ void __launch_bounds__(kFThreads, 1)
                     if (!ok) break;
                     tc::mma_commit(&tfull[acc]);
                     last_bar = &tfull[acc];
-                    last_par = (g >> 1) & 1u;
+                    last_par = (g / kFAcc) & 1u;
                 }
                 if (!ok) break;
                 tc::mma_commit(&bempty[ib]);  // the B buffer is free once this item's MMAs complete
@@ -344,18 +347,25 @@ __global__ void __launch_bounds__(kFThreads, 1)
             for (int o = 16; o > 0; o >>= 1) pcap += __shfl_xor_sync(TB_FULL, pcap, o);
             for (int j = ew; j < n; j += kFEpiWarps) {
                 const float* qr = a.qrot + (int64_t)a.pair_q[pstart + j] * D_pad;
+                // one pass over the dims: lane l holds w_d for d = 4 l + 128 i + k (D_pad <= 256)
+                double wv[kFMaxDPad / 128][4];
                 double wmax = 0.0, bsq = 0.0;
-                for (int d0 = 4 * lane; d0 < D_pad; d0 += 128) {
-                    const float4 v4 = *reinterpret_cast<const float4*>(vm + d0);
-                    const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr + d0));
-                    const float4 d4 = *reinterpret_cast<const float4*>(dl + d0);
-                    const double bv[4] = {(double)v4.x - q4.x, (double)v4.y - q4.y, (double)v4.z - q4.z,
-                                          (double)v4.w - q4.w};
-                    const double dv[4] = {d4.x, d4.y, d4.z, d4.w};
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        wmax = fmax(wmax, fabs(dv[k] * bv[k]));
-                        bsq += bv[k] * bv[k];
+                for (int i = 0; i < kFMaxDPad / 128; ++i) {
+                    const int d0 = 4 * lane + 128 * i;
+                    if (d0 < D_pad) {
+                        const float4 v4 = *reinterpret_cast<const float4*>(vm + d0);
+                        const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr + d0));
+                        const float4 d4 = *reinterpret_cast<const float4*>(dl + d0);
+                        const double bv[4] = {(double)v4.x - q4.x, (double)v4.y - q4.y, (double)v4.z - q4.z,
+                                              (double)v4.w - q4.w};
+                        const double dv[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            wv[i][k] = dv[k] * bv[k];
+                            wmax = fmax(wmax, fabs(wv[i][k]));
+                            bsq += bv[k] * bv[k];
+                        }
                     }
                 }
 #pragma unroll
@@ -366,29 +376,27 @@ __global__ void __launch_bounds__(kFThreads, 1)
                 const double sig = wmax > 0.0 ? wmax / 127.0 : 1.0;
                 const double inv = 1.0 / sig;
                 double rmax = 0.0;
-                for (int d0 = 4 * lane; d0 < D_pad; d0 += 128) {
-                    const float4 v4 = *reinterpret_cast<const float4*>(vm + d0);
-                    const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr + d0));
-                    const float4 d4 = *reinterpret_cast<const float4*>(dl + d0);
-                    const double bv[4] = {(double)v4.x - q4.x, (double)v4.y - q4.y, (double)v4.z - q4.z,
-                                          (double)v4.w - q4.w};
-                    const double dv[4] = {d4.x, d4.y, d4.z, d4.w};
-                    uint32_t hw = 0, lw = 0;
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        // any split is valid: the residual is measured below against the exact w
-                        const double w = dv[k] * bv[k];
-                        const double h = fmin(fmax(rint(w * inv), -127.0), 127.0);
-                        const double r = w - sig * h;
-                        const double l = fmin(fmax(rint(r * inv * 254.0), -127.0), 127.0);
-                        rmax = fmax(rmax, fabs(r - sig * l / 254.0));
-                        hw |= ((uint32_t)(int32_t)h & 0xFFu) << (8 * k);
-                        lw |= ((uint32_t)(int32_t)l & 0xFFu) << (8 * k);
+                for (int i = 0; i < kFMaxDPad / 128; ++i) {
+                    const int d0 = 4 * lane + 128 * i;
+                    if (d0 < D_pad) {
+                        uint32_t hw = 0, lw = 0;
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            // any split is valid: the residual is measured below against the exact w
+                            const double w = wv[i][k];
+                            const double h = fmin(fmax(rint(w * inv), -127.0), 127.0);
+                            const double r = w - sig * h;
+                            const double l = fmin(fmax(rint(r * inv * 254.0), -127.0), 127.0);
+                            rmax = fmax(rmax, fabs(r - sig * l / 254.0));
+                            hw |= ((uint32_t)(int32_t)h & 0xFFu) << (8 * k);
+                            lw |= ((uint32_t)(int32_t)l & 0xFFu) << (8 * k);
+                        }
+                        const int b = d0 >> 5, kk = d0 & 31;
+                        unsigned char* blk = bb + (size_t)b * a.b_stride;
+                        *reinterpret_cast<uint32_t*>(blk + sw32_off(2 * j, kk)) = hw;
+                        *reinterpret_cast<uint32_t*>(blk + sw32_off(2 * j + 1, kk)) = lw;
                     }
-                    const int b = d0 >> 5, kk = d0 & 31;
-                    unsigned char* blk = bb + (size_t)b * a.b_stride;
-                    *reinterpret_cast<uint32_t*>(blk + sw32_off(2 * j, kk)) = hw;
-                    *reinterpret_cast<uint32_t*>(blk + sw32_off(2 * j + 1, kk)) = lw;
                 }
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) rmax = fmax(rmax, __shfl_xor_sync(TB_FULL, rmax, o));
@@ -453,14 +461,14 @@ __global__ void __launch_bounds__(kFThreads, 1)
             const int jb = part * qper;
             const int jn = max(0, min(n, jb + qper) - jb);
             for (int s = 0; s < ns; ++s, ++g) {
-                const int acc = g & 1;
+                const int acc = g & (kFAcc - 1);
                 const int rl = s * kFM + quarter * 32 + lane;  // list-local row of this lane
                 const bool valid = rl < L;
                 const int64_t tile = t0 + s / sub_per_tile;
                 const int slot = (s % sub_per_tile) * kFM + quarter * 32 + lane;
                 // the row term is loaded before the wait, so its latency overlaps it
                 const float P = (valid && live) ? __ldg(a.rowp + tile * T + slot) : 0.0f;
-                const bool w = live && tc::bar_wait(&tfull[acc], (g >> 1) & 1u, a.polls, abort_flag);
+                const bool w = live && tc::bar_wait(&tfull[acc], (g / kFAcc) & 1u, a.polls, abort_flag);
                 if (!__all_sync(TB_FULL, w)) stop();
                 if (!live) continue;
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
