@@ -408,13 +408,15 @@ def cpu_baseline(args, cfg, xq, c_np, xs, perm, off, n_max):
                       f"omp_cpu_ivfflat_f32 with {threads} threads), {dt:.2f}s"}
 
 
-def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks, list_stride=0):
+def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks, list_stride=0, tensor=False):
     """Algorithmic bytes of the scan launch under each query's final K-th distance, divided by its
     measured duration. bytes = B*D_pad*4 (rotated queries) + per distinct probed list (4 B per row id
     + 3*D_pad*4 B of vmin/delta/eps) + per row 32 B x the largest number of 32-dim blocks any query
     must scan + D*4 B per distinct surviving row + 8 B per candidate slot written.
     list_stride > 1 profiles only the lists c with c % list_stride == 0 (all queries probing them)
-    and scales the per-row terms by the probed rows' total over the sampled lists' rows."""
+    and scales the per-row terms by the probed rows' total over the sampled lists' rows.
+    tensor: the scan ran Stage Y on the tensor cores (filter_kernel), which reads every code block of
+    a probed row where the algorithm needs only the blocks above; the bytes stay the algorithm's."""
     import numpy as np
     import torch
 
@@ -467,8 +469,11 @@ def roofline(idx, cfg, xq_dev, out_d, scan_ms, peaks, list_stride=0):
     achieved = bytes_alg / (scan_ms * 1e-3) / 1e9
     peak = float(peaks.get("hbm_gbs", 6650.0))
     out = {
-        "bound": "hbm", "kernel": "scan_kernel (Stage Y/Z over every probe)", "achieved": round(achieved, 1),
-        "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic_from_profile(cfg.name),
+        "bound": "hbm",
+        "kernel": ("filter_kernel (Stage Y on the tensor cores, Stage Z, every probe)" if tensor
+                   else "scan_kernel (Stage Y/Z over every probe)"),
+        "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+        "traffic": traffic_from_profile(cfg.name, "filter_kernel" if tensor else "scan_kernel"),
         "algorithmic_bytes": int(bytes_alg), "launch_ms": round(scan_ms, 4),
         "peak_source": "measured (MEASURED_PEAKS.json hbm_gbs)" if "hbm_gbs" in peaks else "fallback 6.65 TB/s",
         "pairs": int((p1 >= 0).sum()), "candidates": int(round(cand.sum() * scale)),
@@ -525,13 +530,13 @@ def pcie_accounting(idx, cfg, xq_dev, nprobe, K, mode, ub_seed, ms_per_step, d=N
             "pcie_frac": round(gbs / best, 4) if best > 0 else None}
 
 
-def traffic_from_profile(workload: str):
-    """DRAM bytes per scan launch at `workload` from the committed ncu summary of that workload
+def traffic_from_profile(workload: str, kernel: str = "scan_kernel"):
+    """DRAM bytes per launch of `kernel` at `workload` from the committed ncu summary of that kernel
     (a line `dram_bytes_per_launch[<workload>]: <bytes>`), or None when no capture of it is committed."""
     import glob
 
     key = f"dram_bytes_per_launch[{workload}]:"
-    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", "scan_kernel_*.md"))):
+    for path in sorted(glob.glob(os.path.join(ROOT, "profiles", f"{kernel}_*.md"))):
         for line in open(path):
             if line.strip().startswith(key):
                 try:
@@ -709,7 +714,8 @@ def run_ours(args, d: Dist):
         if not args.no_roofline and mode == 2:
             # rank 0's scan covers every rank's queries over rank 0's lists
             stride = 64 if cfg.nlist > 8192 else 1
-            roof = roofline(idx, cfg, xq_all_dev, d_all, scan_ms, peaks, list_stride=stride)
+            roof = roofline(idx, cfg, xq_all_dev, d_all, scan_ms, peaks, list_stride=stride,
+                            tensor=idx.stage_y_tensor(B * d.world, nprobe, K, args.ub_seed))
             if d.world > 1:
                 roof["scope"] = f"rank 0's scan: all {B * d.world} queries over rank 0's lists"
         cpu = None
@@ -812,7 +818,8 @@ def run_sweep(args, d: Dist):
                     row[f"check_{name}"] = bool(np.array_equal(ii[:m].cpu().numpy(), oi) and
                                                 np.array_equal(dd[:m].cpu().numpy().view(np.uint32), od.view(np.uint32)))
                     if mode == 2 and B <= 100:
-                        r = roofline(idx, ds_cfg_with(cfg, B=B, nprobe=nprobe, K=K), q, dd.cpu().numpy(), scan_ms, peaks)
+                        r = roofline(idx, ds_cfg_with(cfg, B=B, nprobe=nprobe, K=K), q, dd.cpu().numpy(), scan_ms, peaks,
+                                     tensor=idx.stage_y_tensor(B, nprobe, K))
                         row["cascade_scan_roofline_frac"] = r["frac"]
                         row["cascade_scan_alg_bytes"] = r["algorithmic_bytes"]
                         row["cascade_scan_ms"] = round(scan_ms, 4)

@@ -133,6 +133,10 @@ int32_t trident_p_init(int32_t mode, int32_t B, int32_t K, int32_t nprobe);
  * TRIDENT_ROUTE_W0_B200. */
 int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, double w0);
 
+/* 1 when a cascade search of this shape (mode 2, ub_seed 0 or 1) runs Stage Y on the tensor cores,
+ * 0 when it runs the CUDA-core Stage Y (no reference counterpart: the reference has one Stage Y). */
+int32_t trident_stage_y_tensor(const trident_index* idx, int32_t B, int32_t K, int32_t nprobe, int32_t ub_seed);
+
 /* The whole query path, replacing launch_trident_v4_search (:1172-1604). The cascade runs as
  * coarse stage -> Stage X seed (each query's threshold from the best rows of its nearest lists,
  * ranked by a partial SQ8 distance) -> one Stage Y/Z scan over every probe -> merge, where the

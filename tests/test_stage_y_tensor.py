@@ -130,3 +130,25 @@ def test_tensor_stage_y_waits_that_give_up_mark_every_result():
     finally:
         _lib.set_wait_limits(-1, -1)
     torch.cuda.synchronize()
+
+
+def test_stage_y_path_query():
+    """trident_stage_y_tensor: the size rule (D_pad <= 256, B * nprobe >= 32768), the flag that forces
+    the tensor cores, and what keeps the CUDA cores (no row_p, UB seeding inside items, K > 128)."""
+    from trident_b200 import _lib
+
+    f = load_case("g1_int_c1")  # D = 128
+    idx = build_index(f, device="cpu")
+    assert not idx.stage_y_tensor(48, 4)
+    assert idx.stage_y_tensor(1000, 64)
+    assert not idx.stage_y_tensor(1000, 64, ub_seed=2)
+    assert not idx.stage_y_tensor(1000, 64, k=129)
+    idx.set_stage_y("always")
+    assert idx.stage_y_tensor(48, 4)
+    idx.set_stage_y("off")
+    assert not idx.stage_y_tensor(1000, 64)
+    idx.set_stage_y("auto")
+    d = idx.desc()
+    wide = type(d).from_buffer_copy(d)
+    wide.D, wide.D_pad, wide.num_blocks = 960, 960, 30
+    assert _lib.lib().trident_stage_y_tensor(wide, 1000, 10, 64, 0) == 0

@@ -27,7 +27,7 @@ EXPORTED = (
     "trident_route", "trident_search", "trident_search_profiled", "trident_launch_count", "trident_coarse",
     "trident_merge_shards", "trident_search_noalloc", "trident_search_prep", "trident_search_seed",
     "trident_search_finish", "trident_workspace_status", "trident_set_wait_limits",
-    "trident_noalloc_workspace_bytes", "trident_assign",
+    "trident_noalloc_workspace_bytes", "trident_assign", "trident_stage_y_tensor",
 )
 QINFO_LEN = 4
 PHASES = ("coarse", "pairs", "seed", "scan", "merge")
@@ -100,6 +100,8 @@ def lib():
     L.trident_p_init.restype = i32
     L.trident_route.argtypes = [DP, i32, i32, ctypes.c_double]
     L.trident_route.restype = i32
+    L.trident_stage_y_tensor.argtypes = [DP, i32, i32, i32, i32]
+    L.trident_stage_y_tensor.restype = i32
     L.trident_search.argtypes = [DP, P, i32, i32, i32, i32, i32, P, sz, P, P, P, P]
     L.trident_search_profiled.argtypes = [DP, P, i32, i32, i32, i32, i32, P, sz, P, P, P, P, P]
     L.trident_launch_count.restype = i64

@@ -165,6 +165,11 @@ int32_t trident_route(const trident_index* idx, int32_t B, int32_t nprobe, doubl
     return W < w0 ? TRIDENT_MODE_CM_FP32 : TRIDENT_MODE_CASCADE;
 }
 
+int32_t trident_stage_y_tensor(const trident_index* idx, int32_t B, int32_t K, int32_t nprobe, int32_t ub_seed) {
+    if (!idx || B < 0 || nprobe < 1) return 0;
+    return filter_eligible(*idx, K, true, ub_seed == 2, (int64_t)B * nprobe) ? 1 : 0;
+}
+
 static int check_search_args(const trident_index* idx, const float* xq, int32_t B, int32_t K, int32_t nprobe,
                              void* workspace, size_t workspace_bytes, Workspace* ws) {
     int rc = trident_index_check(idx);

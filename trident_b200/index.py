@@ -371,6 +371,10 @@ class TridentV4Index:
         value was 9e8."""
         return int(_lib.lib().trident_route(self.desc(), int(B), int(nprobe), float(w0)))
 
+    def stage_y_tensor(self, B: int, nprobe: int, k: int = 10, ub_seed: int = 0) -> bool:
+        """Whether a cascade search of this shape runs Stage Y on the tensor cores (else CUDA cores)."""
+        return bool(_lib.lib().trident_stage_y_tensor(self.desc(), int(B), int(k), int(nprobe), int(ub_seed)))
+
     def search(self, xq_gpu, nprobe: int, mode: int = 2, use_l1: int = 0, rerank_m: int = 0, tile_override: int = 0,
                warp_refine: int = 1, stats_buf=None, record_kernel_ms: bool = False, k: int = 10, ub_seed: int = 0,
                out=None, phase_ms: Optional[dict] = None):
