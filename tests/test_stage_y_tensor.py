@@ -77,6 +77,8 @@ def test_forced_tensor_stage_y_equals_oracle_on_fixtures(name, K):
     ("c4", dict(N=1_000_000, nlist=656, nprobe=256, B=1000, K=10, n_comp=41)),
     # c3 shape: unit-norm real rows, D = 96 (D_pad 96: three code blocks)
     ("c3", dict(N=500_000, nlist=1024, nprobe=32, B=2000, K=10)),
+    # c2 shape: D = 960, the wide variant (Hi and Lo converted separately), 256-row tiles
+    ("c2", dict(N=200_000, nlist=1024, nprobe=64, B=1000, K=10)),
 ])
 def test_tensor_and_cuda_core_stage_y_agree_at_config_shapes(cfg_name, over):
     from trident_b200 import datasets as ds

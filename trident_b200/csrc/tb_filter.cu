@@ -12,7 +12,8 @@
 // Hi = sum code_d hi_d and Lo = sum code_d lo_d are integer dot products of the u8 codes with s8
 // weights that tcgen05.mma.kind::i8 accumulates exactly in int32 (A = 128 rows of codes, B = the
 // item's queries as N = 2n columns hi, lo). The epilogue evaluates per (row, query)
-//   v = (P_r + Bsq_j) + (2 s_j / 254) (254 Hi + Lo)      (D_pad <= 256, so 254 Hi + Lo fits int32)
+//   v = (P_r + Bsq_j) + (2 s_j / 254) (254 Hi + Lo)      (D_pad <= 256, so 254 Hi + Lo fits int32;
+//                                                         above, 2 s_j Hi + (2 s_j / 254) Lo)
 // in float32; v - slack_j is a lower bound of ||x^ - q~||^2, where slack_j covers the quantisation
 // residual (2 R_j 255 D_pad) and every float32 rounding (8 u times a bound of each term's size).
 // With E_c = ||eps_c||_2 >= ||x~ - x^|| (eps bounds each dim), the triangle inequality gives
@@ -67,7 +68,8 @@ constexpr uint32_t kFTmemCols = kFAcc * kFMaxN; // all 512 columns: one CTA per 
 constexpr int kFSmemLimit = 227 * 1024;
 constexpr int kFStatic = 8 * 1024;             // static shared memory and reserve
 constexpr double kU = 5.9604644775390625e-08;  // float32 unit roundoff 2^-24
-constexpr int kFMaxDPad = 256;                 // 254 Hi + Lo stays within int32
+constexpr int kFNarrowDPad = 256;              // up to here 254 Hi + Lo stays within int32
+constexpr int kFMaxDPad = 1024;                // beyond 256, Hi and Lo are converted separately
 constexpr int64_t kFMinPairs = 32768;          // (query, list) pairs of a search that picks this path
 
 struct FilterArgs {
@@ -145,7 +147,7 @@ __device__ __forceinline__ float phi_of(float ts, double E, double slack) {
     return f32_up(s * s * (1.0 + 1e-12) + slack);
 }
 
-template <int KM, bool VEC4>
+template <int KM, bool VEC4, bool WIDE>
 __global__ void __launch_bounds__(kFThreads, 1)
     filter_kernel(const __grid_constant__ CUtensorMap mcodes, const FilterArgs a) {
     extern __shared__ unsigned char f_smem_raw[];
@@ -153,7 +155,8 @@ __global__ void __launch_bounds__(kFThreads, 1)
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     // per B buffer (the item it was built for): per-query weight constants
-    __shared__ float2 s_qc[2][kFMaxG];     // {c_x = 2 s_j / 254, base = Bsq rounded down}
+    __shared__ float2 s_qc[2][kFMaxG];     // {c_x = 2 s_j / 254 (WIDE: c_hi = 2 s_j), base = Bsq rounded down}
+    __shared__ float s_qlo[2][kFMaxG];     // WIDE: c_lo = 2 s_j / 254
     __shared__ double s_slack[2][kFMaxG];  // slack_j
     __shared__ double s_ec[2];             // E_c
     // the item being tested
@@ -347,24 +350,36 @@ __global__ void __launch_bounds__(kFThreads, 1)
             for (int o = 16; o > 0; o >>= 1) pcap += __shfl_xor_sync(TB_FULL, pcap, o);
             for (int j = ew; j < n; j += kFEpiWarps) {
                 const float* qr = a.qrot + (int64_t)a.pair_q[pstart + j] * D_pad;
-                // one pass over the dims: lane l holds w_d for d = 4 l + 128 i + k (D_pad <= 256)
-                double wv[kFMaxDPad / 128][4];
+                // lane l covers d = 4 l + 128 i + k; up to D_pad = 256 its weights stay in registers
+                // between the two steps, above they are recomputed from a second read
+                constexpr int kHeld = WIDE ? 1 : kFNarrowDPad / 128;
+                double wv[kHeld][4];
+                auto weights = [&](int i, double* w4, double* b4) {
+                    const int d0 = 4 * lane + 128 * i;
+                    const float4 v4 = *reinterpret_cast<const float4*>(vm + d0);
+                    const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr + d0));
+                    const float4 d4 = *reinterpret_cast<const float4*>(dl + d0);
+                    b4[0] = (double)v4.x - q4.x;
+                    b4[1] = (double)v4.y - q4.y;
+                    b4[2] = (double)v4.z - q4.z;
+                    b4[3] = (double)v4.w - q4.w;
+                    w4[0] = (double)d4.x * b4[0];
+                    w4[1] = (double)d4.y * b4[1];
+                    w4[2] = (double)d4.z * b4[2];
+                    w4[3] = (double)d4.w * b4[3];
+                };
+                const int nch = (D_pad + 127) / 128;
                 double wmax = 0.0, bsq = 0.0;
 #pragma unroll
-                for (int i = 0; i < kFMaxDPad / 128; ++i) {
-                    const int d0 = 4 * lane + 128 * i;
-                    if (d0 < D_pad) {
-                        const float4 v4 = *reinterpret_cast<const float4*>(vm + d0);
-                        const float4 q4 = __ldg(reinterpret_cast<const float4*>(qr + d0));
-                        const float4 d4 = *reinterpret_cast<const float4*>(dl + d0);
-                        const double bv[4] = {(double)v4.x - q4.x, (double)v4.y - q4.y, (double)v4.z - q4.z,
-                                              (double)v4.w - q4.w};
-                        const double dv[4] = {d4.x, d4.y, d4.z, d4.w};
+                for (int i = 0; i < (WIDE ? kFMaxDPad / 128 : kFNarrowDPad / 128); ++i) {
+                    if (i < nch && 4 * lane + 128 * i < D_pad) {
+                        double w4[4], b4[4];
+                        weights(i, w4, b4);
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
-                            wv[i][k] = dv[k] * bv[k];
-                            wmax = fmax(wmax, fabs(wv[i][k]));
-                            bsq += bv[k] * bv[k];
+                            if (!WIDE) wv[WIDE ? 0 : i][k] = w4[k];
+                            wmax = fmax(wmax, fabs(w4[k]));
+                            bsq += b4[k] * b4[k];
                         }
                     }
                 }
@@ -377,14 +392,21 @@ __global__ void __launch_bounds__(kFThreads, 1)
                 const double inv = 1.0 / sig;
                 double rmax = 0.0;
 #pragma unroll
-                for (int i = 0; i < kFMaxDPad / 128; ++i) {
+                for (int i = 0; i < (WIDE ? kFMaxDPad / 128 : kFNarrowDPad / 128); ++i) {
                     const int d0 = 4 * lane + 128 * i;
-                    if (d0 < D_pad) {
+                    if (i < nch && d0 < D_pad) {
+                        double w4[4], b4[4];
+                        if (WIDE) {
+                            weights(i, w4, b4);
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < 4; ++k) w4[k] = wv[WIDE ? 0 : i][k];
+                        }
                         uint32_t hw = 0, lw = 0;
 #pragma unroll
                         for (int k = 0; k < 4; ++k) {
                             // any split is valid: the residual is measured below against the exact w
-                            const double w = wv[i][k];
+                            const double w = w4[k];
                             const double h = fmin(fmax(rint(w * inv), -127.0), 127.0);
                             const double r = w - sig * h;
                             const double l = fmin(fmax(rint(r * inv * 254.0), -127.0), 127.0);
@@ -408,7 +430,12 @@ __global__ void __launch_bounds__(kFThreads, 1)
                     const double mag = pcap + bsq + xmag;
                     s_slack[buf][j] = 8.0 * kU * mag + 2.0 * rmax * cmax;
                     const float base = f32_down(bsq * (1.0 - 1e-12));
-                    s_qc[buf][j] = make_float2((float)(2.0 * sig / 254.0), base);
+                    if (WIDE) {
+                        s_qc[buf][j] = make_float2((float)(2.0 * sig), base);
+                        s_qlo[buf][j] = (float)(2.0 * sig / 254.0);
+                    } else {
+                        s_qc[buf][j] = make_float2((float)(2.0 * sig / 254.0), base);
+                    }
                 }
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the tensor core reads B
@@ -493,8 +520,9 @@ __global__ void __launch_bounds__(kFThreads, 1)
                         for (int i = 0; i < 8; ++i) {
                             if (g8 + i < jn) {
                                 const float2 qc = s_qc[ib][jb + g8 + i];
-                                const float v =
-                                    fmaf(qc.x, (float)((int32_t)r[2 * i] * 254 + (int32_t)r[2 * i + 1]), P + qc.y);
+                                const int32_t hi = (int32_t)r[2 * i], lo = (int32_t)r[2 * i + 1];
+                                const float v = WIDE ? fmaf(s_qlo[ib][jb + g8 + i], (float)lo, fmaf(qc.x, (float)hi, P + qc.y))
+                                                     : fmaf(qc.x, (float)(hi * 254 + lo), P + qc.y);
                                 const unsigned mk = __ballot_sync(TB_FULL, valid && v <= s_phi[jb + g8 + i]);
                                 if (mk) {
                                     nz |= 1u << (g8 + i);
@@ -604,9 +632,9 @@ size_t filter_smem(const trident_index& idx, int K, int G) {
            (size_t)G * km_of(K) * (sizeof(float) + sizeof(int32_t));
 }
 
-template <int KM, bool VEC4>
+template <int KM, bool VEC4, bool WIDE>
 cudaError_t launch_t(const CUtensorMap& map, const FilterArgs& a, size_t smem, int grid, cudaStream_t st) {
-    auto kern = filter_kernel<KM, VEC4>;
+    auto kern = filter_kernel<KM, VEC4, WIDE>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     kern<<<grid, kFThreads, smem, st>>>(map, a);
@@ -626,7 +654,8 @@ bool filter_eligible(const trident_index& idx, int K, bool lb, bool ub_items, in
     if (idx.tile_size % kFM != 0 || idx.D_pad % 32 != 0 || idx.D_pad > kFMaxDPad) return false;
     // measured on B200: faster than scan_kernel at c3 / c4 shapes, slower with few pairs (the
     // items' operand set-up is not amortised) or at D = 960 (c2)
-    if (!(idx.flags & TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS) && pairs < kFMinPairs) return false;
+    if (!(idx.flags & TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS) && (pairs < kFMinPairs || idx.D_pad > kFNarrowDPad))
+        return false;
     // every code row of the 2-D view must have a 32-bit coordinate
     const int64_t max_tiles = idx.N / idx.tile_size + idx.nlist + 1;
     if (max_tiles * idx.num_blocks * idx.tile_size >= ((int64_t)1 << 31)) return false;
@@ -677,8 +706,18 @@ cudaError_t launch_filter(const trident_index& idx, const float* xq, const Works
     if (grid > sl.max_items) grid = sl.max_items;
     const bool vec4 = (idx.D % 4) == 0 && (((uintptr_t)idx.xb_sorted | (uintptr_t)xq) & 15) == 0;
     const int KM = km_of(sl.K);
-    if (KM == 32) return vec4 ? launch_t<32, true>(map, a, smem, grid, st) : launch_t<32, false>(map, a, smem, grid, st);
-    if (KM == 128) return vec4 ? launch_t<128, true>(map, a, smem, grid, st) : launch_t<128, false>(map, a, smem, grid, st);
+    const bool wide = idx.D_pad > kFNarrowDPad;
+#define TB_FILTER_CASE(km, v, w) \
+    if (KM == km && vec4 == v && wide == w) return launch_t<km, v, w>(map, a, smem, grid, st);
+    TB_FILTER_CASE(32, true, false)
+    TB_FILTER_CASE(32, false, false)
+    TB_FILTER_CASE(128, true, false)
+    TB_FILTER_CASE(128, false, false)
+    TB_FILTER_CASE(32, true, true)
+    TB_FILTER_CASE(32, false, true)
+    TB_FILTER_CASE(128, true, true)
+    TB_FILTER_CASE(128, false, true)
+#undef TB_FILTER_CASE
     return cudaErrorInvalidValue;
 }
 
