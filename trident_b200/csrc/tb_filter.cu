@@ -71,6 +71,7 @@ constexpr double kU = 5.9604644775390625e-08;  // float32 unit roundoff 2^-24
 constexpr int kFNarrowDPad = 256;              // up to here 254 Hi + Lo stays within int32
 constexpr int kFMaxDPad = 1024;                // beyond 256, Hi and Lo are converted separately
 constexpr int64_t kFMinPairs = 32768;          // (query, list) pairs of a search that picks this path
+constexpr int kFMaxAutoK = 32;                 // above, each item's K insertions per query dominate
 
 struct FilterArgs {
     const float* xb;
@@ -652,9 +653,11 @@ int filter_group_size(const trident_index& idx, int K) {
 bool filter_eligible(const trident_index& idx, int K, bool lb, bool ub_items, int64_t pairs) {
     if (!lb || ub_items || idx.row_p == nullptr || K > 128) return false;
     if (idx.tile_size % kFM != 0 || idx.D_pad % 32 != 0 || idx.D_pad > kFMaxDPad) return false;
-    // measured on B200: faster than scan_kernel at c3 / c4 shapes, slower with few pairs (the
-    // items' operand set-up is not amortised) or at D = 960 (c2)
-    if (!(idx.flags & TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS) && (pairs < kFMinPairs || idx.D_pad > kFNarrowDPad))
+    // measured on B200: faster than scan_kernel at c3 / c4 shapes for K <= 10, slower with few pairs
+    // (the items' operand set-up is not amortised), at D = 960 (c2) and for K = 50 / 100 (the
+    // refinements of each item's first K rows per query, one warp and one lock at a time)
+    if (!(idx.flags & TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS) &&
+        (pairs < kFMinPairs || idx.D_pad > kFNarrowDPad || K > kFMaxAutoK))
         return false;
     // every code row of the 2-D view must have a 32-bit coordinate
     const int64_t max_tiles = idx.N / idx.tile_size + idx.nlist + 1;
