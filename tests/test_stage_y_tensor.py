@@ -155,3 +155,71 @@ def test_stage_y_path_query():
     wide = type(d).from_buffer_copy(d)
     wide.D, wide.D_pad, wide.num_blocks = 960, 960, 30
     assert _lib.lib().trident_stage_y_tensor(wide, 1000, 10, 64, 0) == 0
+
+
+def _f32(x):
+    return np.asarray(x, np.float64).astype(np.float32)
+
+
+def _f32_down(x):
+    """The largest float32 <= x (x >= 0)."""
+    f = np.float32(x)
+    return np.nextafter(f, np.float32(0)) if float(f) > x else f
+
+
+def _fma32(a, b, c):
+    """float32 fma: the exact float64 product of two float32 values, plus c, rounded once."""
+    return _f32(np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64))
+
+
+@pytest.mark.parametrize("name", CASE_NAMES)
+def test_tensor_bound_never_exceeds_the_dequantised_distance(name):
+    """The tensor-core Stage Y's value v (filter_kernel, restated here: float64 split weights with a
+    measured residual, exact integer dot products, the kernel's float32 evaluation order) minus its
+    slack is a lower bound of ||x^ - q~||^2 for every probed (query, row) pair of the fixture."""
+    from oracle import oracle as O
+
+    f = load_case(name)
+    idx = build_index(f, device="cpu")
+    h = idx.host_arrays()
+    T, D_pad, nb, D = idx.tile_size, idx.D_pad, idx.num_blocks, idx.D
+    vec_off, tile_off = h["vec_off"], h["tile_off"]
+    codes = h["codes"].reshape(-1, nb, T, 32).transpose(0, 2, 1, 3).reshape(-1, T, D_pad)
+    rowp = idx.row_p().numpy()
+    qrot = O.rotate_f64(f["xq"], f["mean64"], f["R64"], D_pad)
+    probe, _ = O.probe_select_f64(f["xq"], f["centroids"], int(f["nprobe"]))
+    u = 2.0 ** -24
+    checked = 0
+    for qi in range(qrot.shape[0]):
+        for c in probe[qi]:
+            L = int(vec_off[c + 1] - vec_off[c])
+            if L == 0:
+                continue
+            nt = (L + T - 1) // T
+            cd = codes[tile_off[c]:tile_off[c] + nt].reshape(-1, D_pad)[:L].astype(np.int64)
+            P = rowp[tile_off[c] * T + np.arange(L)]
+            vm = h["vmin"][c].astype(np.float64)
+            dl = h["delta"][c].astype(np.float64)
+            b = vm - qrot[qi].astype(np.float64)
+            w = dl * b
+            sig = np.abs(w).max() / 127.0 if np.abs(w).max() > 0 else 1.0
+            hi = np.clip(np.rint(w * (1.0 / sig)), -127, 127)
+            r = w - sig * hi
+            lo = np.clip(np.rint(r * (1.0 / sig) * 254.0), -127, 127)
+            rmax = np.abs(r - sig * lo / 254.0).max() * (1 + 1e-9) + sig * 1e-12
+            Hi, Lo = cd @ hi.astype(np.int64), cd @ lo.astype(np.int64)
+            bsq = float((b * b).sum())
+            pcap = float(((255.0 * dl) ** 2).sum())
+            cmax = 255.0 * D_pad
+            slack = 8 * u * (pcap + bsq + 2 * sig * 127 * cmax * (1 + 1 / 254)) + 2 * rmax * cmax
+            base = _f32_down(bsq * (1 - 1e-12))
+            s1 = _f32(P.astype(np.float64) + float(base))
+            if D_pad <= 256:
+                v = _fma32(_f32(2 * sig / 254), _f32(254 * Hi + Lo), s1)
+            else:
+                v = _fma32(_f32(2 * sig / 254), _f32(Lo), _fma32(_f32(2 * sig), _f32(Hi), s1))
+            xhat = vm + cd * dl
+            exact = ((xhat - qrot[qi].astype(np.float64)) ** 2).sum(axis=1)
+            assert (v.astype(np.float64) - slack <= exact).all(), (qi, c)
+            checked += L
+    assert checked > 0
