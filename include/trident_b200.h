@@ -81,14 +81,14 @@ typedef struct trident_index {
     /* Optional [total_tiles * tile_size], in code-slot order (tile t, row v of the tile): the row's
      * sum_d (code_d delta_d)^2 in float64, rounded down to float (0 for empty slots). With it the
      * cascade runs Stage Y on the tensor cores (an 8-bit MMA per 32-dim code block and a bound over
-     * all dims at once) when D_pad <= 256, K <= 32 and B * nprobe >= 32768, where it is the faster
+     * all dims at once) when D_pad <= 256 and B * nprobe >= 32768, where it is the faster
      * (or always, with TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS); NULL keeps the CUDA-core Stage Y.
      * Results are the same either way. */
     const float*   row_p;
 } trident_index;
 
 /* trident_index.flags: run Stage Y on the tensor cores for every cascade search (given row_p),
- * not only where the library's size rule picks it (D_pad <= 256, K <= 32, B * nprobe >= 32768). */
+ * not only where the library's size rule picks it (D_pad <= 256, B * nprobe >= 32768). */
 #define TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS 1
 
 /* Statistics slots of the optional int64 `stats` array (at least TRIDENT_STATS_LEN entries, zeroed

@@ -135,7 +135,7 @@ def test_tensor_stage_y_waits_that_give_up_mark_every_result():
 
 
 def test_stage_y_path_query():
-    """trident_stage_y_tensor: the size rule (D_pad <= 256, K <= 32, B * nprobe >= 32768), the flag that forces
+    """trident_stage_y_tensor: the size rule (D_pad <= 256, B * nprobe >= 32768), the flag that forces
     the tensor cores, and what keeps the CUDA cores (no row_p, UB seeding inside items, K > 128)."""
     from trident_b200 import _lib
 
@@ -145,7 +145,7 @@ def test_stage_y_path_query():
     assert idx.stage_y_tensor(1000, 64)
     assert not idx.stage_y_tensor(1000, 64, ub_seed=2)
     assert not idx.stage_y_tensor(1000, 64, k=129)
-    assert not idx.stage_y_tensor(1000, 64, k=50)
+    assert idx.stage_y_tensor(1000, 64, k=100)
     idx.set_stage_y("always")
     assert idx.stage_y_tensor(48, 4)
     idx.set_stage_y("off")

@@ -21,7 +21,8 @@
 //   v > Phi_j = (sqrt(ts_j) + E_c)^2 + slack_j,
 // with ts_j the same prune threshold (prune_threshold: tau, the query's sigma, rho) as the
 // CUDA-core Stage Y. Survivors are refined at once (exact FP32, the reference's summation order)
-// and inserted into the item's per-query top-K under a bounded per-query lock; a list that fills
+// and inserted into the item's per-query top-K under a bounded per-query lock, all of a query's
+// survivors among a warp's 32 rows with one lock and one list insertion; a list that fills
 // lowers the query's threshold for this CTA (Phi_j) and, through the per-query atomicMin, for the
 // whole GPU. At the item's end its lists go to the (query, probe) candidate slots the merge reads,
 // exactly like scan_kernel's.
@@ -71,7 +72,6 @@ constexpr double kU = 5.9604644775390625e-08;  // float32 unit roundoff 2^-24
 constexpr int kFNarrowDPad = 256;              // up to here 254 Hi + Lo stays within int32
 constexpr int kFMaxDPad = 1024;                // beyond 256, Hi and Lo are converted separately
 constexpr int64_t kFMinPairs = 32768;          // (query, list) pairs of a search that picks this path
-constexpr int kFMaxAutoK = 32;                 // above, each item's K insertions per query dominate
 
 struct FilterArgs {
     const float* xb;
@@ -542,51 +542,56 @@ __global__ void __launch_bounds__(kFThreads, 1)
                     const int i = __ffs(nz) - 1;
                     nz &= nz - 1;
                     const int j = jb + i;
-                    unsigned m = s_msk[ew][i];
-                    while (m) {  // refine each survivor (whole warp) and insert it under the lock
-                        const int sl = __ffs(m) - 1;
-                        m &= m - 1;
-                        if (lane == 0) ++st_surv;
+                    const unsigned m = s_msk[ew][i];
+                    const int q = s_qid[j];
+                    // every survivor's exact distance (whole warp each), kept by the survivor's own lane
+                    float my_d = kInf;
+                    for (unsigned mm = m; mm;) {
+                        const int sl = __ffs(mm) - 1;
+                        mm &= mm - 1;
                         const int64_t grow = r0 + (int64_t)(s * kFM + quarter * 32 + sl);
-                        const int q = s_qid[j];
                         const float dist = exact_dist_warp<VEC4, 2>(a.xb + grow * D, a.xq + (int64_t)q * D, D, lane);
-                        const int32_t id = __ldg(a.oid + grow);
-                        int got = 0;
-                        if (lane == 0) {
-                            for (uint32_t spin = 0; spin < a.lock_spins; ++spin) {
-                                if (atomicCAS(&s_lock[j], 0, 1) == 0) {
-                                    got = 1;
-                                    break;
-                                }
-                                __nanosleep(64);
+                        const float d0 = __shfl_sync(TB_FULL, dist, 0);
+                        if (lane == sl) my_d = d0;
+                    }
+                    const bool mine = (m >> lane) & 1u;
+                    const int32_t my_id = mine ? __ldg(a.oid + r0 + (int64_t)(s * kFM + quarter * 32 + lane)) : -1;
+                    if (lane == 0) st_surv += (unsigned)__popc(m);
+                    // one insertion of all of them under the query's lock
+                    int got = 0;
+                    if (lane == 0) {
+                        for (uint32_t spin = 0; spin < a.lock_spins; ++spin) {
+                            if (atomicCAS(&s_lock[j], 0, 1) == 0) {
+                                got = 1;
+                                break;
                             }
+                            __nanosleep(64);
                         }
-                        got = __shfl_sync(TB_FULL, got, 0);
-                        if (!got) {
-                            if (lane == 0) atomicOr(a.err, TRIDENT_STATUS_LOCK_TIMEOUT);
-                            continue;
+                    }
+                    got = __shfl_sync(TB_FULL, got, 0);
+                    if (!got) {
+                        if (lane == 0) atomicOr(a.err, TRIDENT_STATUS_LOCK_TIMEOUT);
+                        continue;
+                    }
+                    __threadfence_block();
+                    float* ld = s_topd + j * KM;
+                    int32_t* li = s_topi + j * KM;
+                    const int ins = list_offer<KM>(ld, li, K, mine, my_d, my_id, lane);
+                    if (lane == 0) {
+                        st_ins += (unsigned)ins;
+                        const float kth = ld[K - 1];
+                        const float gq = ld_volatile_f32(a.tau + q);
+                        const float t_old = s_tau[j];
+                        const float tq = fminf(fminf(t_old, kth), gq);
+                        if (tq < t_old) {
+                            s_tau[j] = tq;
+                            s_phi[j] = phi_of(prune_threshold(tq, s_sig[j], a.rho), E, s_slack[ib][j]);
                         }
                         __threadfence_block();
-                        float* ld = s_topd + j * KM;
-                        int32_t* li = s_topi + j * KM;
-                        const float d0 = __shfl_sync(TB_FULL, dist, 0);
-                        const int ins = list_offer<KM>(ld, li, K, lane == 0, d0, id, lane);
-                        if (lane == 0) {
-                            st_ins += (unsigned)ins;
-                            const float kth = ld[K - 1];
-                            const float gq = ld_volatile_f32(a.tau + q);
-                            const float t_old = s_tau[j];
-                            const float tq = fminf(fminf(t_old, kth), gq);
-                            if (tq < t_old) {
-                                s_tau[j] = tq;
-                                s_phi[j] = phi_of(prune_threshold(tq, s_sig[j], a.rho), E, s_slack[ib][j]);
-                            }
-                            __threadfence_block();
-                            atomicExch(&s_lock[j], 0);
-                            if (kth < t_old && kth < gq) atomicMin(a.tau + q, __float_as_uint(kth));
-                        }
-                        __syncwarp();
+                        atomicExch(&s_lock[j], 0);
+                        if (kth < t_old && kth < gq) atomicMin(a.tau + q, __float_as_uint(kth));
                     }
+                    __syncwarp();
                 }
             }
             epi_sync();
@@ -653,11 +658,9 @@ int filter_group_size(const trident_index& idx, int K) {
 bool filter_eligible(const trident_index& idx, int K, bool lb, bool ub_items, int64_t pairs) {
     if (!lb || ub_items || idx.row_p == nullptr || K > 128) return false;
     if (idx.tile_size % kFM != 0 || idx.D_pad % 32 != 0 || idx.D_pad > kFMaxDPad) return false;
-    // measured on B200: faster than scan_kernel at c3 / c4 shapes for K <= 10, slower with few pairs
-    // (the items' operand set-up is not amortised), at D = 960 (c2) and for K = 50 / 100 (the
-    // refinements of each item's first K rows per query, one warp and one lock at a time)
-    if (!(idx.flags & TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS) &&
-        (pairs < kFMinPairs || idx.D_pad > kFNarrowDPad || K > kFMaxAutoK))
+    // measured on B200: faster than scan_kernel at c3 / c4 shapes (K = 10 and 100), slower with few
+    // pairs (the items' operand set-up is not amortised) and at D = 960 (c2)
+    if (!(idx.flags & TRIDENT_INDEX_TENSOR_STAGE_Y_ALWAYS) && (pairs < kFMinPairs || idx.D_pad > kFNarrowDPad))
         return false;
     // every code row of the 2-D view must have a 32-bit coordinate
     const int64_t max_tiles = idx.N / idx.tile_size + idx.nlist + 1;

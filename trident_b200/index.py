@@ -268,7 +268,7 @@ class TridentV4Index:
     # ------------------------------------------------------------------------------------------
     # Stage Y on the tensor cores (the library's tcgen05 8-bit filter) needs each code slot's
     # sum_d (code_d delta_d)^2 (row_p). "auto" lets the library pick it where it is the faster
-    # (D_pad <= 256, K <= 32, B * nprobe >= 32768), "always" for every cascade search, "off" never. The
+    # (D_pad <= 256, B * nprobe >= 32768), "always" for every cascade search, "off" never. The
     # results are identical in every setting.
     stage_y = "auto"
 
