@@ -174,22 +174,19 @@ def _fma32(a, b, c):
     return _f32(np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64))
 
 
-@pytest.mark.parametrize("name", CASE_NAMES)
-def test_tensor_bound_never_exceeds_the_dequantised_distance(name):
-    """The tensor-core Stage Y's value v (filter_kernel, restated here: float64 split weights with a
-    measured residual, exact integer dot products, the kernel's float32 evaluation order) minus its
-    slack is a lower bound of ||x^ - q~||^2 for every probed (query, row) pair of the fixture."""
+def _check_tensor_bound(idx, xq, centroids, mean64, R64, nprobe):
+    """Restates filter_kernel's value v (float64 split weights with a measured residual, exact integer
+    dot products, the kernel's float32 evaluation order) and asserts v - slack <= ||x^ - q~||^2 for
+    every probed (query, row) pair. Returns the number of pairs checked."""
     from oracle import oracle as O
 
-    f = load_case(name)
-    idx = build_index(f, device="cpu")
     h = idx.host_arrays()
-    T, D_pad, nb, D = idx.tile_size, idx.D_pad, idx.num_blocks, idx.D
+    T, D_pad, nb = idx.tile_size, idx.D_pad, idx.num_blocks
     vec_off, tile_off = h["vec_off"], h["tile_off"]
     codes = h["codes"].reshape(-1, nb, T, 32).transpose(0, 2, 1, 3).reshape(-1, T, D_pad)
     rowp = idx.row_p().numpy()
-    qrot = O.rotate_f64(f["xq"], f["mean64"], f["R64"], D_pad)
-    probe, _ = O.probe_select_f64(f["xq"], f["centroids"], int(f["nprobe"]))
+    qrot = O.rotate_f64(xq, mean64, R64, D_pad)
+    probe, _ = O.probe_select_f64(xq, centroids, nprobe)
     u = 2.0 ** -24
     checked = 0
     for qi in range(qrot.shape[0]):
@@ -224,4 +221,34 @@ def test_tensor_bound_never_exceeds_the_dequantised_distance(name):
             exact = ((xhat - qrot[qi].astype(np.float64)) ** 2).sum(axis=1)
             assert (v.astype(np.float64) - slack <= exact).all(), (qi, c)
             checked += L
-    assert checked > 0
+    return checked
+
+
+@pytest.mark.parametrize("name", CASE_NAMES)
+def test_tensor_bound_never_exceeds_the_dequantised_distance(name):
+    """On every fixture, v - slack of the tensor-core Stage Y is a lower bound of ||x^ - q~||^2."""
+    f = load_case(name)
+    idx = build_index(f, device="cpu")
+    assert _check_tensor_bound(idx, f["xq"], f["centroids"], f["mean64"], f["R64"], int(f["nprobe"])) > 0
+
+
+@pytest.mark.parametrize("D,offset,spread", [
+    (960, 0.0, 1.0),      # the wide evaluation (Hi and Lo converted separately)
+    (128, 3.0e4, 0.05),   # far from the origin, tiny spread: P, ||b||^2 and the cross term cancel
+    (256, -1.0e3, 40.0),  # the largest narrow D_pad, mixed signs
+])
+def test_tensor_bound_holds_under_cancellation_and_wide_rows(D, offset, spread):
+    from trident_b200 import SharedClusterStorage, TridentV4Index
+
+    rng = np.random.default_rng(11)
+    nlist, N = 8, 1600
+    cent = (offset + spread * 20 * rng.standard_normal((nlist, D))).astype(np.float32)
+    lids = rng.integers(0, nlist, N).astype(np.int32)
+    xb = (cent[lids] + spread * rng.standard_normal((N, D))).astype(np.float32)
+    xq = (cent[rng.integers(0, nlist, 12)] + spread * rng.standard_normal((12, D))).astype(np.float32)
+    mean64 = np.zeros(D)
+    R64 = np.linalg.qr(rng.standard_normal((D, D)))[0]
+    st = SharedClusterStorage(xb, lids, None, nlist, device="cpu")
+    idx = TridentV4Index(st, cent, mean64, R64, tile_size=128 if D < 256 else 256, device="cpu", max_batch=12,
+                         max_nprobe=4)
+    assert _check_tensor_bound(idx, xq, cent, mean64, R64, 4) > 0
