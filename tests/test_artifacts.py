@@ -28,6 +28,8 @@ def test_save_load_round_trip_on_the_host(tmp_path, name, rows_dtype):
     for k in ("N", "D", "D_pad", "nlist", "tile_size", "num_blocks", "total_tiles", "centroid_norm_max",
               "lb_rel_slack"):
         assert getattr(got, k) == getattr(idx, k), k
+    # the tensor-core Stage Y's row terms come out the same from the loaded codes and deltas
+    assert np.array_equal(got.row_p().numpy(), idx.row_p().numpy())
     # the C ABI accepts the loaded descriptor
     d = got.desc()
     assert d.N == idx.N and d.nlist == idx.nlist
